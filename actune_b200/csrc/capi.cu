@@ -1,0 +1,314 @@
+// extern "C" boundary of libactune_b200.so (declared in include/actune_b200.h).
+//
+// Validation mirrors the reference's checks (actune/kernels/grouped_native.cu:92-105,
+// grouped.py:117-119): bit widths in {2,4,8}, K a multiple of 64, matching
+// shapes; violations return a status instead of throwing across the ABI.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "../../include/actune_b200.h"
+#include "kernels.cuh"
+
+namespace actune {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  std::atomic<int> state{0};  // 0 unknown, 1 ok, 2 unsupported
+  int num_sms = 0;
+};
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_init_mutex;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int current_device(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ACTUNE_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return ACTUNE_ERR_DEVICE;
+  DeviceInfo& d = g_devices[dev];
+  int st = d.state.load(std::memory_order_acquire);
+  if (st == 0) {
+    std::lock_guard<std::mutex> lock(g_init_mutex);
+    st = d.state.load(std::memory_order_relaxed);
+    if (st == 0) {
+      int major = 0, minor = 0, sms = 0;
+      if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return ACTUNE_ERR_CUDA;
+      if (g_encode == nullptr) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || fn == nullptr)
+          return ACTUNE_ERR_CUDA;
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+      }
+      d.num_sms = sms;
+      st = (major == 10 && minor == 0) ? 1 : 2;
+      d.state.store(st, std::memory_order_release);
+    }
+  }
+  if (st != 1) return ACTUNE_ERR_DEVICE;
+  *dev_out = dev;
+  return ACTUNE_OK;
+}
+
+bool valid_bits(int b) { return b == 2 || b == 4 || b == 8; }
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+bool valid_float_dtype(int t) { return t == ACTUNE_DTYPE_F32 || t == ACTUNE_DTYPE_F16 || t == ACTUNE_DTYPE_BF16; }
+size_t dtype_size(int t) { return t == ACTUNE_DTYPE_F32 ? 4 : 2; }
+
+// 2D uint8 tensor map [rows, row_bytes] with a box of [box_rows, box_bytes].
+int encode_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows,
+               bool swizzle128) {
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
+int pick_bn(int variant, int64_t M, int64_t N, int num_sms) {
+  switch (variant) {
+    case ACTUNE_VARIANT_BN32: return 32;
+    case ACTUNE_VARIANT_BN64: return 64;
+    case ACTUNE_VARIANT_BN128: return 128;
+    default: break;
+  }
+  // Minimise waves x tile width (time per tile grows with BN); prefer wider
+  // tiles on ties (fewer re-reads of the activation tile).
+  const int64_t mt = (M + 127) / 128;
+  int best = 128;
+  int64_t best_cost = INT64_MAX;
+  for (int bn : {128, 64, 32}) {
+    const int64_t tiles = mt * ((N + bn - 1) / bn);
+    const int64_t waves = (tiles + num_sms - 1) / num_sms;
+    const int64_t cost = waves * bn;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <int W, int A>
+cudaError_t dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, cudaStream_t s) {
+  switch (bn) {
+    case 32: return launch_group64_gemm<W, A, 32>(ta, tw, p, s);
+    case 64: return launch_group64_gemm<W, A, 64>(ta, tw, p, s);
+    default: return launch_group64_gemm<W, A, 128>(ta, tw, p, s);
+  }
+}
+
+cudaError_t dispatch_gemm(int W, int A, int bn, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
+                          cudaStream_t s) {
+#define ACTUNE_CASE(WW, AA) \
+  if (W == WW && A == AA) return dispatch_bn<WW, AA>(bn, ta, tw, p, s);
+  ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
+  ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
+  ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
+#undef ACTUNE_CASE
+  return cudaErrorInvalidValue;
+}
+
+int check_gemm_shape(int64_t M, int64_t N, int64_t K, int W, int A) {
+  if (!valid_bits(W) || !valid_bits(A)) return ACTUNE_ERR_INVALID_VALUE;
+  if (K <= 0 || K % 64 || K > (int64_t(1) << 24)) return ACTUNE_ERR_INVALID_VALUE;
+  if (M < 0 || N < 0 || M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31)) return ACTUNE_ERR_INVALID_VALUE;
+  return ACTUNE_OK;
+}
+
+int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const float* w_scale, const void* bias,
+             int bias_dtype, void* out, int out_dtype, int32_t* dots, int64_t M, int64_t N, int64_t K, int W, int A,
+             int variant, cudaStream_t stream) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != ACTUNE_OK) return rc;
+  if (M == 0 || N == 0) return ACTUNE_OK;
+  if (!aligned(a, 16) || !aligned(w, 16)) return ACTUNE_ERR_MISALIGNED;
+  const int bn = pick_bn(variant, M, N, g_devices[dev].num_sms);
+  CUtensorMap ta, tw;
+  rc = encode_map(&ta, a, M, K * A / 8, A == 8 ? 128 : 16 * A, 128, A == 8);
+  if (rc != ACTUNE_OK) return rc;
+  rc = encode_map(&tw, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn, W == 8);
+  if (rc != ACTUNE_OK) return rc;
+  GemmParams p{};
+  p.act_scale = a_scale;
+  p.w_scale = w_scale;
+  p.bias = bias;
+  p.out = out;
+  p.dots = dots;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.G = (int)(K / 64);
+  p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
+  p.out_dtype = out_dtype;
+  p.out_vec_ok = (N % 8 == 0) && aligned(out, 16);
+  return dispatch_gemm(W, A, bn, ta, tw, p, stream) == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
+}  // namespace
+}  // namespace actune
+
+using namespace actune;
+
+extern "C" {
+
+int actune_abi_version(void) { return ACTUNE_ABI_VERSION; }
+
+const char* actune_status_string(int status) {
+  switch (status) {
+    case ACTUNE_OK: return "ok";
+    case ACTUNE_ERR_INVALID_VALUE: return "invalid value (shape, bit width, dtype or null pointer)";
+    case ACTUNE_ERR_MISALIGNED: return "misaligned pointer";
+    case ACTUNE_ERR_DEVICE: return "current CUDA device is not an sm_100 (B200-class) GPU";
+    case ACTUNE_ERR_CUDA: return "CUDA runtime/driver call failed";
+    case ACTUNE_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+int actune_quantize_group64(const void* x, int x_dtype, int64_t M, int64_t K, int A, uint8_t* packed, float* scales,
+                            void* stream) {
+  if (!valid_bits(A) || !valid_float_dtype(x_dtype) || M < 0 || K <= 0 || K % 64) return ACTUNE_ERR_INVALID_VALUE;
+  if (M > 0 && (x == nullptr || packed == nullptr || scales == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != ACTUNE_OK) return rc;
+  if (M == 0) return ACTUNE_OK;
+  if (!aligned(x, 16) || !aligned(packed, 8) || !aligned(scales, 4)) return ACTUNE_ERR_MISALIGNED;
+  const int dt = x_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (x_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
+  cudaError_t e = launch_quantize_group64(x, dt, M * (K / 64), A, packed, scales, g_devices[dev].num_sms,
+                                          reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
+int actune_packed_linear(const uint8_t* a, const float* a_scale, const uint8_t* w, const float* w_scale,
+                         const void* bias, int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                         int W, int A, int variant, void* stream) {
+  int rc = check_gemm_shape(M, N, K, W, A);
+  if (rc != ACTUNE_OK) return rc;
+  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_BN128) return ACTUNE_ERR_INVALID_VALUE;
+  if (bias != nullptr && !valid_float_dtype(bias_dtype)) return ACTUNE_ERR_INVALID_VALUE;
+  if (M > 0 && N > 0 && (a == nullptr || a_scale == nullptr || w == nullptr || w_scale == nullptr || out == nullptr))
+    return ACTUNE_ERR_INVALID_VALUE;
+  if (!aligned(a_scale, 4) || !aligned(w_scale, 4) || !aligned(out, dtype_size(out_dtype)) ||
+      (bias != nullptr && !aligned(bias, dtype_size(bias_dtype))))
+    return ACTUNE_ERR_MISALIGNED;
+  const int bdt = bias == nullptr ? kDtNone
+                                  : (bias_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16
+                                                                     : (bias_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32));
+  const int odt = out_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (out_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
+  return run_gemm(a, a_scale, w, w_scale, bias, bdt, out, odt, nullptr, M, N, K, W, A, variant,
+                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+int actune_packed_linear_dots(const uint8_t* a, const uint8_t* w, int32_t* dots, int64_t M, int64_t N, int64_t K,
+                              int W, int A, int variant, void* stream) {
+  int rc = check_gemm_shape(M, N, K, W, A);
+  if (rc != ACTUNE_OK) return rc;
+  if (variant < 0 || variant > ACTUNE_VARIANT_BN128) return ACTUNE_ERR_INVALID_VALUE;
+  if (M > 0 && N > 0 && (a == nullptr || w == nullptr || dots == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
+  if (!aligned(dots, 4)) return ACTUNE_ERR_MISALIGNED;
+  return run_gemm(a, nullptr, w, nullptr, nullptr, kDtNone, nullptr, kDtF32, dots, M, N, K, W, A, variant,
+                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+int actune_weight_codes(const void* weight, int dtype, int64_t N, int64_t K, int W, int A, const float* clip,
+                        int8_t* codes, float* scale, void* stream) {
+  if (!valid_bits(W) || !valid_bits(A) || !valid_float_dtype(dtype) || N < 0 || K <= 0 || N >= (int64_t(1) << 31))
+    return ACTUNE_ERR_INVALID_VALUE;
+  if (N > 0 && (weight == nullptr || codes == nullptr || scale == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != ACTUNE_OK) return rc;
+  if (!aligned(weight, dtype_size(dtype)) || !aligned(scale, 4) || (clip != nullptr && !aligned(clip, 4)))
+    return ACTUNE_ERR_MISALIGNED;
+  const int dt = dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
+  cudaError_t e = launch_weight_codes(weight, dt, N, K, W, A, clip, codes, scale, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
+int actune_r4_refine(const void* weight, int dtype, int64_t N, int64_t K, const int8_t* q4, const float* scale4,
+                     int8_t* residual, int8_t* q8, void* stream) {
+  if (!valid_float_dtype(dtype) || N < 0 || K <= 0 || N >= (int64_t(1) << 31)) return ACTUNE_ERR_INVALID_VALUE;
+  if (N > 0 && (weight == nullptr || q4 == nullptr || scale4 == nullptr || residual == nullptr || q8 == nullptr))
+    return ACTUNE_ERR_INVALID_VALUE;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != ACTUNE_OK) return rc;
+  if (!aligned(weight, dtype_size(dtype)) || !aligned(scale4, 4)) return ACTUNE_ERR_MISALIGNED;
+  const int dt = dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
+  cudaError_t e = launch_r4_refine(weight, dt, N, K, q4, scale4, residual, q8, reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
+int actune_pack_rows(const int8_t* codes, int64_t R, int64_t K, int bits, uint8_t* packed, void* stream) {
+  if (!valid_bits(bits) || R < 0 || K <= 0 || K % (8 / bits)) return ACTUNE_ERR_INVALID_VALUE;
+  if (R > 0 && (codes == nullptr || packed == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != ACTUNE_OK) return rc;
+  cudaError_t e = launch_pack_rows(codes, R * (K * bits / 8), bits, packed, g_devices[dev].num_sms,
+                                   reinterpret_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
+size_t actune_grouped_linear_workspace_size(int64_t M, int64_t K, int A) {
+  if (M <= 0 || K <= 0 || !valid_bits(A)) return 0;
+  const size_t packed = ((size_t)M * (size_t)K * (size_t)A / 8 + 255) / 256 * 256;
+  const size_t scales = ((size_t)M * (size_t)(K / 64) * 4 + 255) / 256 * 256;
+  return packed + scales;
+}
+
+int actune_grouped_linear(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* w, const float* w_scale,
+                          const void* bias, int bias_dtype, int64_t N, int W, int A, void* out, int out_dtype,
+                          void* workspace, size_t workspace_bytes, int variant, void* stream) {
+  int rc = check_gemm_shape(M, N, K, W, A);
+  if (rc != ACTUNE_OK) return rc;
+  if (M == 0 || N == 0) {
+    int dev = 0;
+    return current_device(&dev);
+  }
+  const size_t need = actune_grouped_linear_workspace_size(M, K, A);
+  if (workspace == nullptr || workspace_bytes < need) return ACTUNE_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return ACTUNE_ERR_MISALIGNED;
+  uint8_t* packed = reinterpret_cast<uint8_t*>(workspace);
+  float* scales = reinterpret_cast<float*>(packed + ((size_t)M * (size_t)K * (size_t)A / 8 + 255) / 256 * 256);
+  rc = actune_quantize_group64(x, x_dtype, M, K, A, packed, scales, stream);
+  if (rc != ACTUNE_OK) return rc;
+  return actune_packed_linear(packed, scales, w, w_scale, bias, bias_dtype, out, out_dtype, M, N, K, W, A, variant,
+                              stream);
+}
+
+int actune_device_error(int* code, int* site, int reset) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != ACTUNE_OK) return rc;
+  if (cudaDeviceSynchronize() != cudaSuccess) return ACTUNE_ERR_CUDA;
+  int c = 0, s = 0;
+  if (cudaMemcpyFromSymbol(&c, g_actune_error, sizeof(int)) != cudaSuccess ||
+      cudaMemcpyFromSymbol(&s, g_actune_error_site, sizeof(int)) != cudaSuccess)
+    return ACTUNE_ERR_CUDA;
+  if (code) *code = c;
+  if (site) *site = s;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_actune_error, &zero, sizeof(int)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_actune_error_site, &zero, sizeof(int)) != cudaSuccess)
+      return ACTUNE_ERR_CUDA;
+  }
+  return ACTUNE_OK;
+}
+
+}  // extern "C"

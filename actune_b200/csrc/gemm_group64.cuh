@@ -1,0 +1,361 @@
+// Packed-integer group-64 linear on Blackwell tensor cores (sm_100a).
+//
+//   y[m, n] = ws[n] * sum_g ( float(dot_g(m, n)) * as[m, g] )  (+ bias[n])
+//   dot_g(m, n) = sum_{k in group g} a[m, k] * w[n, k]          (exact int32)
+//
+// with the fp32 chain evaluated exactly as the reference's GPU kernels do
+// (actune/kernels/grouped.py:80-94, actune/kernels/grouped_native.cu:70-85):
+// acc = fma(float(dot_g), as[m, g], acc) for g = 0, 1, ... in order, then
+// y = fma(acc, ws[n], bias[n]) (or acc * ws[n] without bias), rounded once to
+// the output type.  Every W x A pair in {2,4,8}^2 runs on tcgen05 kind::i8.
+//
+// CTA tile: 128 token rows (TMEM lanes) x BN weight rows (TMEM columns);
+// K is streamed in stages of 128 (two groups of 64).  Warp roles:
+//   warp 0      TMA producer: packed activation and weight tiles -> smem ring
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer; each 64-wide
+//               group goes into its own TMEM int32 accumulator buffer
+//               (NACC buffers rotate so the epilogue of group g overlaps the
+//               MMAs of groups g+1..)
+//   warps 2-3   converters: sub-byte codes -> int8 in the canonical
+//               128B-swizzled K-major layout (code placed in the top bits of
+//               the byte, i.e. scaled by 2^(8-bits); compensated exactly in fp32)
+//   warps 4..   epilogue: tcgen05.ld of each group's int32 dots, exact
+//               int->fp32 conversion, packed fp32x2 FMA into register
+//               accumulators, final scale/bias/convert/store
+#pragma once
+
+#include "common.cuh"
+
+namespace actune {
+
+enum : int { kDtNone = 0, kDtF32 = 1, kDtF16 = 2, kDtBF16 = 3 };
+
+struct GemmParams {
+  const float* act_scale;  // [M, G]
+  const float* w_scale;    // [N]
+  const void* bias;        // [N] (bias_dtype) or nullptr
+  void* out;               // [M, N] (out_dtype)
+  int32_t* dots;           // debug export [M, N, G] int32 (exact group dots) or nullptr
+  int M, N, K, G;
+  int bias_dtype;
+  int out_dtype;
+  int out_vec_ok;          // N % 8 == 0 and out 16-byte aligned
+};
+
+// Wait-site identifiers recorded with a device timeout.
+enum : int { kSiteProducer = 1, kSiteConverter, kSiteMmaFull, kSiteMmaAcc, kSiteMmaDone, kSiteEpilogue, kSiteDrain };
+
+template <int W, int A, int BN>
+struct Group64Cfg {
+  static_assert(W == 2 || W == 4 || W == 8, "W");
+  static_assert(A == 2 || A == 4 || A == 8, "A");
+  static_assert(BN == 32 || BN == 64 || BN == 128, "BN");
+  static constexpr int BM = 128;     // token rows per tile = TMEM lanes = MMA M
+  static constexpr int KS = 128;     // K elements per pipeline stage (two groups)
+  static constexpr int EPI_WG = 2;                // two epilogue warpgroups split the columns
+  static constexpr int COLS = BN / EPI_WG;      // accumulator columns per epilogue thread
+  static constexpr int THREADS = 128 + 128 * EPI_WG;
+  static constexpr int NACC = BN == 32 ? 8 : 4;    // TMEM int32 accumulator buffers
+  static constexpr int TMEM_COLS = NACC * BN;      // 256 or 512 (power of two)
+  static constexpr bool CONVERT = (A < 8) || (W < 8);
+  // Per-stage shared-memory layout: [act int8 | wgt int8 | act packed | wgt packed].
+  static constexpr int OP_A_BYTES = BM * KS;        // 16 KB, SW128 K-major
+  static constexpr int OP_W_BYTES = BN * KS;
+  static constexpr int STG_A_BYTES = A < 8 ? BM * KS * A / 8 : 0;
+  static constexpr int STG_W_BYTES = W < 8 ? BN * KS * W / 8 : 0;
+  static constexpr int STAGE_RAW = OP_A_BYTES + OP_W_BYTES + STG_A_BYTES + STG_W_BYTES;
+  static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
+  static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+  // Bytes one stage's two TMA loads deliver (full boxes; OOB parts are zero-filled).
+  static constexpr uint32_t TX_BYTES = BM * KS * A / 8 + BN * KS * W / 8;
+  // int8 operand value = code * 2^(8-bits): the dot carries 2^SHIFT.
+  static constexpr int SHIFT = (8 - A) + (8 - W);
+  static_assert(STAGES >= 2, "stages");
+};
+
+// Unpack one stage of packed sub-byte codes (ROWS rows x 128 codes, row pitch
+// 16*BITS bytes) into the SW128 K-major int8 operand (row pitch 128 bytes,
+// 16-byte chunk c of row r stored at chunk c ^ (r mod 8)).
+template <int BITS, int ROWS>
+__device__ __forceinline__ void unpack_stage(const uint8_t* __restrict__ stg, uint8_t* __restrict__ op, int tid,
+                                             int nthreads) {
+#pragma unroll 4
+  for (int item = tid; item < ROWS * 8; item += nthreads) {
+    const int r = item >> 3, c = item & 7;
+    uint4 v;
+    if constexpr (BITS == 4) {
+      const uint2 src = *reinterpret_cast<const uint2*>(stg + r * 64 + c * 8);
+      const uint2 lo = unpack_w4_word(src.x), hi = unpack_w4_word(src.y);
+      v = make_uint4(lo.x, lo.y, hi.x, hi.y);
+    } else {
+      const uint32_t src = *reinterpret_cast<const uint32_t*>(stg + r * 32 + c * 4);
+      v = unpack_w2_word(src);
+    }
+    *reinterpret_cast<uint4*>(op + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) = v;
+  }
+}
+
+__device__ __forceinline__ float load_bias(const void* bias, int dtype, int n) {
+  if (dtype == kDtF32) return __ldg(reinterpret_cast<const float*>(bias) + n);
+  if (dtype == kDtBF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(bias)[n]);
+  return __half2float(reinterpret_cast<const __half*>(bias)[n]);
+}
+
+__device__ __forceinline__ float finish(float acc, const GemmParams& p, int n) {
+  const float ws = __ldg(p.w_scale + n);
+  if (p.bias_dtype != kDtNone) return fmaf(acc, ws, load_bias(p.bias, p.bias_dtype, n));
+  return acc * ws;
+}
+
+__device__ __forceinline__ void store_scalar(const GemmParams& p, int64_t idx, float y) {
+  if (p.out_dtype == kDtBF16) reinterpret_cast<__nv_bfloat16*>(p.out)[idx] = __float2bfloat16_rn(y);
+  else if (p.out_dtype == kDtF16) reinterpret_cast<__half*>(p.out)[idx] = __float2half_rn(y);
+  else reinterpret_cast<float*>(p.out)[idx] = y;
+}
+
+template <int W, int A, int BN>
+__global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
+    group64_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
+                        const GemmParams p) {
+  using C = Group64Cfg<W, A, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_raw[C::STAGES];
+  __shared__ __align__(8) uint64_t full_op[C::STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t acc_full[C::NACC];
+  __shared__ __align__(8) uint64_t acc_empty[C::NACC];
+  __shared__ __align__(8) uint64_t mma_done;
+  __shared__ uint32_t tmem_holder;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G;
+  const int n_iters = (G + 1) >> 1;
+  const int m0 = blockIdx.x * C::BM;
+  const int n0 = blockIdx.y * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_raw[s], 1);
+      mbar_init(&full_op[s], 2);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < C::NACC; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4 * C::EPI_WG);
+    }
+    mbar_init(&mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tm_act);
+    prefetch_tensormap(&tm_wgt);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int it = 0; it < n_iters; ++it) {
+        const int s = it % C::STAGES;
+        if (!mbar_wait(&empty_bar[s], ((it / C::STAGES) & 1) ^ 1, kSiteProducer)) break;
+        uint8_t* st = smem + s * C::STAGE_BYTES;
+        uint8_t* dst_a = (A < 8) ? st + C::OP_A_BYTES + C::OP_W_BYTES : st;
+        uint8_t* dst_w = (W < 8) ? st + C::OP_A_BYTES + C::OP_W_BYTES + C::STG_A_BYTES : st + C::OP_A_BYTES;
+        mbar_arrive_expect_tx(&full_raw[s], C::TX_BYTES);
+        tma_load_2d(dst_a, &tm_act, it * (C::KS * A / 8), m0, &full_raw[s]);
+        tma_load_2d(dst_w, &tm_wgt, it * (C::KS * W / 8), n0, &full_raw[s]);
+        ++issued;
+      }
+      // Never leave the CTA with bulk copies still landing in shared memory.
+      for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it)
+        mbar_wait(&full_raw[it % C::STAGES], (it / C::STAGES) & 1, kSiteDrain);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(C::BM, BN);
+      int g = 0;
+      bool ok = true;
+      for (int it = 0; it < n_iters && ok; ++it) {
+        const int s = it % C::STAGES;
+        uint64_t* ready = C::CONVERT ? &full_op[s] : &full_raw[s];
+        if (!mbar_wait(ready, (it / C::STAGES) & 1, kSiteMmaFull)) break;
+        tc_fence_after();
+        const uint32_t op_a = smem_u32(smem + s * C::STAGE_BYTES);
+        const uint32_t op_w = op_a + C::OP_A_BYTES;
+        for (int gi = 0; gi < 2 && g < G; ++gi, ++g) {
+          const int b = g % C::NACC;
+          if (!mbar_wait(&acc_empty[b], ((g / C::NACC) & 1) ^ 1, kSiteMmaAcc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem_base + b * BN;
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const uint32_t koff = gi * 64 + kk * 32;
+            mma_i8(d, smem_desc_sw128(op_a + koff), smem_desc_sw128(op_w + koff), idesc, kk);
+          }
+          mma_commit(&acc_full[b]);
+        }
+        if (ok) mma_commit(&empty_bar[s]);
+      }
+      mma_commit(&mma_done);
+      mbar_wait(&mma_done, 0, kSiteMmaDone);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ converters
+    if constexpr (C::CONVERT) {
+      const int ctid = threadIdx.x - 64;
+      for (int it = 0; it < n_iters; ++it) {
+        const int s = it % C::STAGES;
+        if (!mbar_wait(&full_raw[s], (it / C::STAGES) & 1, kSiteConverter)) break;
+        uint8_t* st = smem + s * C::STAGE_BYTES;
+        if constexpr (A < 8) unpack_stage<A, C::BM>(st + C::OP_A_BYTES + C::OP_W_BYTES, st, ctid, 64);
+        if constexpr (W < 8)
+          unpack_stage<W, BN>(st + C::OP_A_BYTES + C::OP_W_BYTES + C::STG_A_BYTES, st + C::OP_A_BYTES, ctid, 64);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_op[s]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 4;
+    const int q = ew & 3;        // TMEM lane quarter this warp may access
+    const int e = ew >> 2;       // column slice
+    const int row = q * 32 + lane;
+    const int m = m0 + row;
+    const bool warp_live = (m0 + q * 32) < p.M;  // any valid token row in this warp
+    const int col0 = n0 + e * C::COLS;
+    const float shift_scale = 1.0f / float(1 << C::SHIFT);
+    const float* as_row = p.act_scale + (int64_t)(m < p.M ? m : 0) * G;
+    (void)col0;
+    float2 acc[C::COLS / 2];
+#pragma unroll
+    for (int j = 0; j < C::COLS / 2; ++j) acc[j] = make_float2(0.f, 0.f);
+    const bool load_scales = warp_live && m < p.M && p.dots == nullptr;
+    float s_next = load_scales ? __ldg(as_row) : 0.f;
+    bool ok = true;
+    for (int g = 0; g < G; ++g) {
+      const int b = g % C::NACC;
+      const float s_cur = s_next * shift_scale;
+      if (g + 1 < G) s_next = load_scales ? __ldg(as_row + g + 1) : 0.f;
+      if (!mbar_wait(&acc_full[b], (g / C::NACC) & 1, kSiteEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (warp_live) {
+        uint32_t r[C::COLS];
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + b * BN + e * C::COLS;
+        if constexpr (C::COLS % 32 == 0) {
+#pragma unroll
+          for (int c = 0; c < C::COLS; c += 32) tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < C::COLS; c += 16) tmem_ld16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(&r[c]));
+        }
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+        if (p.dots != nullptr) {
+          if (m < p.M) {
+#pragma unroll
+            for (int j = 0; j < C::COLS; ++j) {
+              const int n = col0 + j;
+              if (n < p.N) p.dots[((int64_t)m * p.N + n) * G + g] = static_cast<int32_t>(r[j]) >> C::SHIFT;
+            }
+          }
+        } else {
+          const float2 s2 = make_float2(s_cur, s_cur);
+          const float2 magic = make_float2(-kMagicValue, -kMagicValue);
+#pragma unroll
+          for (int j = 0; j < C::COLS / 2; ++j) {
+            float2 f = make_float2(__uint_as_float(r[2 * j] + kMagicBits), __uint_as_float(r[2 * j + 1] + kMagicBits));
+            f = fadd2(f, magic);
+            acc[j] = ffma2(f, s2, acc[j]);
+          }
+        }
+      } else {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+      }
+    }
+    // Final epilogue: stage fp32 accumulators through the (now idle) pipeline
+    // shared memory, then every epilogue thread applies ws/bias to 8
+    // consecutive columns of one row and writes them with one coalesced store.
+    if (p.dots == nullptr) {
+      constexpr int LD = BN + 4;  // padded row pitch (floats)
+      float* stage = reinterpret_cast<float*>(smem);
+      if (ok) {
+#pragma unroll
+        for (int j = 0; j < C::COLS / 2; ++j)
+          *reinterpret_cast<float2*>(stage + row * LD + e * C::COLS + 2 * j) = acc[j];
+      }
+      named_barrier_sync(1, 128 * C::EPI_WG);
+      if (ok) {
+        const int et = threadIdx.x - 128;
+        const int rows_here = min(C::BM, p.M - m0);
+        for (int chunk = et; chunk < rows_here * (BN / 8); chunk += 128 * C::EPI_WG) {
+          const int r = chunk / (BN / 8), c8 = (chunk % (BN / 8)) * 8;
+          const int n = n0 + c8;
+          if (n >= p.N) continue;
+          const float4 lo = *reinterpret_cast<const float4*>(stage + r * LD + c8);
+          const float4 hi = *reinterpret_cast<const float4*>(stage + r * LD + c8 + 4);
+          const float a8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+          const int64_t orow = (int64_t)(m0 + r) * p.N;
+          if (p.out_vec_ok && n + 8 <= p.N && p.out_dtype != kDtF32) {
+            float y[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) y[t] = finish(a8[t], p, n + t);
+            uint4 v;
+            if (p.out_dtype == kDtBF16) {
+              __nv_bfloat162 h0 = __floats2bfloat162_rn(y[0], y[1]), h1 = __floats2bfloat162_rn(y[2], y[3]);
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(y[4], y[5]), h3 = __floats2bfloat162_rn(y[6], y[7]);
+              v = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                             *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+            } else {
+              __half2 h0 = __floats2half2_rn(y[0], y[1]), h1 = __floats2half2_rn(y[2], y[3]);
+              __half2 h2 = __floats2half2_rn(y[4], y[5]), h3 = __floats2half2_rn(y[6], y[7]);
+              v = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                             *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+            }
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + orow + n) = v;
+          } else {
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              if (n + t < p.N) store_scalar(p, orow + n + t, finish(a8[t], p, n + t));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// Host-side launch (defined per W in gemm_w*.cu).
+template <int W, int A, int BN>
+cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
+                                cudaStream_t stream);
+
+}  // namespace actune

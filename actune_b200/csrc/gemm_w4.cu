@@ -1,0 +1,39 @@
+// Instantiations of the group-64 tcgen05 GEMM for W = 4 (all A, all tile widths).
+#include "gemm_group64.cuh"
+
+namespace actune {
+
+template <int W, int A, int BN>
+cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
+                                cudaStream_t stream) {
+  using C = Group64Cfg<W, A, BN>;
+  auto kernel = group64_gemm_kernel<W, A, BN>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const dim3 grid((p.M + C::BM - 1) / C::BM, (p.N + BN - 1) / BN);
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
+  return cudaGetLastError();
+}
+
+#define ACTUNE_INST(A, BN)                                                                                  \
+  template cudaError_t launch_group64_gemm<4, A, BN>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, \
+                                                     cudaStream_t);
+ACTUNE_INST(2, 32)
+ACTUNE_INST(2, 64)
+ACTUNE_INST(2, 128)
+ACTUNE_INST(4, 32)
+ACTUNE_INST(4, 64)
+ACTUNE_INST(4, 128)
+ACTUNE_INST(8, 32)
+ACTUNE_INST(8, 64)
+ACTUNE_INST(8, 128)
+#undef ACTUNE_INST
+
+}  // namespace actune

@@ -1,0 +1,17 @@
+// Internal launcher declarations shared by capi.cu and the kernel files.
+#pragma once
+
+#include "gemm_group64.cuh"
+
+namespace actune {
+
+cudaError_t launch_quantize_group64(const void* x, int dtype, int64_t groups, int A, uint8_t* packed, float* scales,
+                                    int num_sms, cudaStream_t stream);
+cudaError_t launch_weight_codes(const void* w, int dtype, int64_t N, int64_t K, int W, int A, const float* clip,
+                                int8_t* codes, float* scale, cudaStream_t stream);
+cudaError_t launch_r4_refine(const void* w, int dtype, int64_t N, int64_t K, const int8_t* q4, const float* scale4,
+                             int8_t* residual, int8_t* q8, cudaStream_t stream);
+cudaError_t launch_pack_rows(const int8_t* q, int64_t total_bytes, int bits, uint8_t* packed, int num_sms,
+                             cudaStream_t stream);
+
+}  // namespace actune

@@ -1,0 +1,79 @@
+"""Bit-exact tile-variant selection (drop-in for the reference's actune/kernels/tuning.py:16-70).
+
+``select(key, launch, configurations, default)`` runs every candidate once,
+keeps only candidates whose output is ``torch.equal`` to the default's, times
+each survivor as a CUDA graph of 10 launches (median of 5 replays) and adopts
+the fastest only if it beats the default by at least 5%.  It refuses to run
+during stream capture, so every key must be warmed before graph capture.
+
+Here the candidates are the library's GEMM tile widths (ACTUNE_VARIANT_BN32 /
+BN64 / BN128).  All of them evaluate the identical fp32 chain, so the
+bit-exactness gate is expected to keep every candidate; it stays as a guard.
+"""
+from __future__ import annotations
+
+import statistics
+
+import torch
+
+from .. import _lib, ops
+
+TUNINGS = {}
+
+
+def select(key, launch, configurations, default):
+    if key in TUNINGS:
+        return TUNINGS[key]["selected"]
+    if torch.cuda.is_current_stream_capturing():
+        raise RuntimeError("Kernel geometry must be warmed before graph capture")
+    expected = launch(default)
+    torch.cuda.synchronize()
+    results = []
+    for config in configurations:
+        result = launch(config)
+        torch.cuda.synchronize()
+        if not torch.equal(expected, result):
+            results.append(dict(config=config, exact=False))
+            continue
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                launch(config)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(10):
+                launch(config)
+        times = []
+        for _ in range(5):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            graph.replay()
+            end.record()
+            end.synchronize()
+            times.append(start.elapsed_time(end) / 10)
+        results.append(dict(config=config, exact=True, ms=statistics.median(times)))
+        del graph
+    valid = [r for r in results if r["exact"]]
+    baseline = next(r for r in valid if r["config"] == default)
+    best = min(valid, key=lambda r: r["ms"])
+    selected = best["config"] if best["ms"] < baseline["ms"] * 0.95 else default
+    TUNINGS[key] = dict(selected=selected, candidates=results)
+    return selected
+
+
+def grouped_forward(self, x):
+    """Replacement GroupedLinear.forward that tunes the GEMM tile per (pair, shape, dtype, bias)."""
+    flat = x.reshape(-1, self.in_features).contiguous()
+    m, k = flat.shape
+    n = self.out_features
+    packed, scales = ops.quantize_group64(flat, self.a)
+
+    def launch(variant):
+        return ops.packed_linear(packed, scales, self.packed_weight, self.weight_scale, self.bias, k, self.w, self.a,
+                                 out_dtype=x.dtype, variant=variant)
+
+    configs = [_lib.VARIANT_AUTO, _lib.VARIANT_BN32, _lib.VARIANT_BN64, _lib.VARIANT_BN128]
+    key = ("grouped", self.w, self.a, m, k, n, str(x.dtype), self.bias is not None)
+    return launch(select(key, launch, configs, _lib.VARIANT_AUTO)).reshape(*x.shape[:-1], n)

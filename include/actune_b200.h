@@ -1,0 +1,136 @@
+/*
+ * actune_b200 -- C ABI of the B200 (sm_100a) group-64 packed-integer linear.
+ *
+ * Plain pointers and sizes only.  Every pointer argument is a device pointer on
+ * the CUDA device that is current on the calling thread, unless noted.  The
+ * caller owns every buffer; no function allocates device memory, so every call
+ * can be captured into a CUDA graph (the first call of each kernel on a device
+ * also sets its shared-memory attribute, so make one call before capturing).
+ * `stream` is a cudaStream_t (NULL = legacy default stream).  All functions are
+ * asynchronous with respect to the host and return an actune_status; a kernel
+ * that fails on the device records the failure in a device word read by
+ * actune_device_error() instead of hanging.
+ *
+ * Bit layouts follow the reference project (paths relative to its root):
+ *   packed activations  uint8 [M, K*A/8], element k of a row at byte k*A/8,
+ *                       bits (k mod 8/A)*A, little-endian    (actune/kernels/grouped.py:55-71)
+ *   activation scales   float [M, K/64]                      (grouped.py:131)
+ *   packed weights      uint8 [N, K*W/8], same bit order     (grouped.py:108-111, 121)
+ *   weight scales       float [N] (one per output row)       (actune/kernels/quantizers.py:23-94)
+ *   bias                [N] bf16/f16/f32, optional           (grouped.py:123-125)
+ *   output              [M, N] bf16/f16/f32                  (grouped.py:138, grouped_native.cu:106)
+ * Constraints: W, A in {2, 4, 8}; K a positive multiple of 64; 0 <= M, N < 2^31;
+ * packed operands 16-byte aligned.
+ */
+#ifndef ACTUNE_B200_H
+#define ACTUNE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ACTUNE_ABI_VERSION 1
+
+typedef enum actune_status {
+  ACTUNE_OK = 0,
+  ACTUNE_ERR_INVALID_VALUE = 1,  /* shape, bit width, dtype code or null pointer rejected */
+  ACTUNE_ERR_MISALIGNED = 2,     /* a pointer violates its alignment requirement */
+  ACTUNE_ERR_DEVICE = 3,         /* the current device is not an sm_100 (B200-class) GPU */
+  ACTUNE_ERR_CUDA = 4,           /* a CUDA runtime or driver call failed (launch, attribute, tensor map) */
+  ACTUNE_ERR_WORKSPACE = 5       /* the workspace passed is smaller than actune_grouped_linear_workspace_size */
+} actune_status;
+
+typedef enum actune_dtype {
+  ACTUNE_DTYPE_NONE = 0,
+  ACTUNE_DTYPE_F32 = 1,
+  ACTUNE_DTYPE_F16 = 2,
+  ACTUNE_DTYPE_BF16 = 3
+} actune_dtype;
+
+/* GEMM tile choice (the reference's `config` argument of grouped_big_m.cu:92-93
+ * selects among its tile geometries the same way).  All variants compute the
+ * identical fp32 chain, so their outputs are bit-identical. */
+typedef enum actune_variant {
+  ACTUNE_VARIANT_AUTO = 0,
+  ACTUNE_VARIANT_BN32 = 1,
+  ACTUNE_VARIANT_BN64 = 2,
+  ACTUNE_VARIANT_BN128 = 3
+} actune_variant;
+
+/* Device error codes reported by actune_device_error(). */
+#define ACTUNE_DEV_OK 0
+#define ACTUNE_DEV_TIMEOUT 1 /* a pipeline wait exceeded its time limit; outputs are invalid */
+
+/* Per-token, per-64-group symmetric activation quantizer and bit packer.
+ * Replaces the Triton `_quantize_groups` launch in GroupedLinear.forward
+ * (actune/kernels/grouped.py:130-133; kernel grouped.py:55-71).
+ * x: [M, K] row-major, dtype x_dtype (BF16, F16 or F32), 16-byte aligned.
+ * packed: uint8 [M, K*A/8] (8-byte aligned); scales: float [M, K/64]. */
+int actune_quantize_group64(const void* x, int x_dtype, int64_t M, int64_t K, int A, uint8_t* packed, float* scales,
+                            void* stream);
+
+/* The packed-integer linear: out = ws * sum_g(float(dot_g) * as[:, g]) (+ bias).
+ * Replaces the native op `linear(a, as, w, ws, bias, source, W, A[, config])`
+ * (actune/kernels/grouped_native.cu:90-115, grouped_big_m.cu:162-205) and the
+ * Triton `_group_gemm` launch (grouped.py:137-142) for all nine W x A pairs.
+ * bias may be NULL (bias_dtype NONE); out_dtype is BF16, F16 or F32. */
+int actune_packed_linear(const uint8_t* a, const float* a_scale, const uint8_t* w, const float* w_scale,
+                         const void* bias, int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                         int W, int A, int variant, void* stream);
+
+/* Debug export of the exact per-group int32 dots: dots[m, n, g] =
+ * sum_{k in group g} a[m,k]*w[n,k], int32 [M, N, K/64].  These are the integer
+ * accumulators of grouped_native.cu:70-74 / grouped.py:89, computed by the same
+ * tensor-core kernel as actune_packed_linear. */
+int actune_packed_linear_dots(const uint8_t* a, const uint8_t* w, int32_t* dots, int64_t M, int64_t N, int64_t K,
+                              int W, int A, int variant, void* stream);
+
+/* Per-row weight codebook (install time).  Replaces
+ * actune/kernels/quantizers.py:83-94 `weight_codes(weight, w, a, clip_ratios)`.
+ * weight: [N, K] dtype BF16/F16/F32; clip: NULL or float [N] ratios in (0, 1]
+ * (validated by the caller as quantizers.py:4-21 does); codes: int8 [N, K];
+ * scale: float [N]. */
+int actune_weight_codes(const void* weight, int dtype, int64_t N, int64_t K, int W, int A, const float* clip,
+                        int8_t* codes, float* scale, void* stream);
+
+/* Nested W8 refinement for given int4 codes and scales.  Replaces
+ * actune/kernels/quantizers.py:42-57 `signed_r4_refine(weight, q4, scale4)`.
+ * weight: [N, K] BF16/F16/F32; q4: int8 [N, K]; scale4: float [N];
+ * residual, q8: int8 [N, K]. */
+int actune_r4_refine(const void* weight, int dtype, int64_t N, int64_t K, const int8_t* q4, const float* scale4,
+                     int8_t* residual, int8_t* q8, void* stream);
+
+/* Little-endian sub-byte row packing.  Replaces actune/kernels/grouped.py:108-111
+ * `pack_rows(q, bits)`.  codes: int8 [R, K]; packed: uint8 [R, K*bits/8]. */
+int actune_pack_rows(const int8_t* codes, int64_t R, int64_t K, int bits, uint8_t* packed, void* stream);
+
+/* Bytes of device workspace actune_grouped_linear needs for (M, K, A). */
+size_t actune_grouped_linear_workspace_size(int64_t M, int64_t K, int A);
+
+/* Whole GroupedLinear.forward for a row-major [M, K] input (quantize + packed
+ * GEMM).  Replaces actune/kernels/grouped.py:127-143.  The packed activations
+ * and their scales live in the caller's `workspace` (256-byte aligned, at least
+ * actune_grouped_linear_workspace_size(M, K, A) bytes). */
+int actune_grouped_linear(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* w, const float* w_scale,
+                          const void* bias, int bias_dtype, int64_t N, int W, int A, void* out, int out_dtype,
+                          void* workspace, size_t workspace_bytes, int variant, void* stream);
+
+/* Human-readable text for an actune_status (static storage). */
+const char* actune_status_string(int status);
+
+/* Reads (and with reset != 0 clears) the device error word of the current
+ * device.  Synchronous: waits for the device's pending work first.
+ * code / site may be NULL. */
+int actune_device_error(int* code, int* site, int reset);
+
+/* ACTUNE_ABI_VERSION of the loaded library. */
+int actune_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ACTUNE_B200_H */

@@ -1,0 +1,241 @@
+"""GPU parity: the sm_100a kernels (through the C ABI) against the pinned CPU oracle.
+
+Bar: bit-exact for everything integer (codes, scales, packed bytes, per-group
+int32 dots) and, because the kernels evaluate the reference GPU kernels' fp32
+chain in the same order (fma per group, then fma with ws and bias), bit-exact
+fp32/bf16 outputs against the oracle in FMA mode.  Against the reference
+interpreter goldens (separate multiply/add) the bf16 outputs must agree within
+max-abs 1e-2 x output RMS (the project's stated tolerance).
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+PAIRS = [(w, a) for w in (2, 4, 8) for a in (2, 4, 8)]
+SHAPES = [(1, 64, 32), (17, 256, 96), (64, 1024, 64)]
+DEV = "cuda"
+
+
+def bf16_bits(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def f32_of_bits(bits):
+    return torch.from_numpy(O.bf16_bits_to_f32(bits).copy())
+
+
+def assert_bits(actual, expected, what):
+    actual = np.ascontiguousarray(actual)
+    expected = np.ascontiguousarray(expected)
+    assert actual.shape == expected.shape, f"{what}: shape {actual.shape} != {expected.shape}"
+    ua = actual.reshape(-1).view(f"u{actual.dtype.itemsize}")
+    ue = expected.reshape(-1).view(f"u{expected.dtype.itemsize}")
+    diff = np.flatnonzero(ua != ue)
+    assert diff.size == 0, f"{what}: {diff.size} of {actual.size} differ, first at {diff[:5]}"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from actune_b200 import _lib, ops as o
+    _lib.device_error(reset=True)
+    yield o
+    code, site = _lib.device_error()
+    assert code == 0, f"device error word {code} (site {site})"
+
+
+@pytest.fixture(scope="module")
+def gemm_golden():
+    return np.load(GOLDEN / "gemm.npz")
+
+
+def inputs(m, k, seed, outliers=True, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(m, k, generator=g)
+    if outliers:
+        cols = torch.randperm(k, generator=torch.Generator().manual_seed(seed))[: max(1, k // 100)]
+        x[:, cols] *= 20.0
+    return x.to(dtype)
+
+
+def weight(n, k, seed):
+    g = torch.Generator().manual_seed(seed + 7)
+    return (torch.randn(n, k, generator=g) * 0.02).bfloat16()
+
+
+# --------------------------------------------------------------------------- quantizer
+@pytest.mark.parametrize("a", [2, 4, 8])
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_quantizer_golden(ops, a, case):
+    q = np.load(GOLDEN / "quantize.npz")
+    x = q[f"a{a}_c{case}_x"]
+    xt = torch.from_numpy(x.view(np.int16).copy()).view(torch.bfloat16) if x.dtype == np.uint16 else torch.from_numpy(x)
+    packed, scales = ops.quantize_group64(xt.to(DEV), a)
+    assert_bits(packed.cpu().numpy(), q[f"a{a}_c{case}_packed"], "packed")
+    assert_bits(scales.cpu().numpy(), q[f"a{a}_c{case}_scales"], "scales")
+
+
+@pytest.mark.parametrize("a", [2, 4, 8])
+@pytest.mark.parametrize("m,k", [(1, 64), (3, 128), (600, 4096), (7, 11008), (129, 16384)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_quantizer_random(ops, a, m, k, dtype):
+    x = inputs(m, k, seed=m * 31 + k + a, dtype=dtype)
+    x[0, :64] = 0  # an all-zero group
+    packed, scales = ops.quantize_group64(x.to(DEV), a)
+    if dtype == torch.bfloat16:
+        ref_p, ref_s = O.quantize_group64(bf16_bits(x), a)
+    else:
+        ref_p, ref_s = O.quantize_group64(x.float().numpy(), a)
+    assert_bits(packed.cpu().numpy(), ref_p, "packed")
+    assert_bits(scales.cpu().numpy(), ref_s, "scales")
+
+
+def test_quantizer_empty(ops):
+    x = torch.empty(0, 128, device=DEV, dtype=torch.bfloat16)
+    packed, scales = ops.quantize_group64(x, 8)
+    assert packed.shape == (0, 128) and scales.shape == (0, 2)
+
+
+# --------------------------------------------------------------------------- weight codes
+@pytest.mark.parametrize("w,a", PAIRS)
+@pytest.mark.parametrize("tag", ["noclip", "clip"])
+def test_weight_codes_golden(ops, w, a, tag):
+    d = np.load(GOLDEN / "weights.npz")
+    wt = torch.from_numpy(d["weight"].view(np.int16).copy()).view(torch.bfloat16).to(DEV)
+    clip = torch.from_numpy(d["clips"]).to(DEV) if tag == "clip" else None
+    from actune_b200.kernels.quantizers import weight_codes
+    codes, scale = weight_codes(wt, w, a, clip_ratios=clip)
+    assert_bits(codes.cpu().numpy(), d[f"w{w}a{a}_{tag}_codes"], "codes")
+    assert_bits(scale.cpu().numpy(), d[f"w{w}a{a}_{tag}_scale"], "scale")
+    packed = ops.pack_rows(codes, w)
+    assert_bits(packed.cpu().numpy(), d[f"w{w}a{a}_{tag}_packed"], "packed")
+
+
+def test_signed_r4_refine_matches_nested_codes(ops):
+    from actune_b200.kernels.quantizers import signed_r4_refine, symmetric_int4_quantize, weight_codes
+    wt = weight(64, 256, 3).to(DEV)
+    q4, s4 = symmetric_int4_quantize(wt)
+    residual, q8 = signed_r4_refine(wt, q4, s4)
+    nested, s8 = weight_codes(wt, 8, 4)
+    assert torch.equal(q8, nested) and torch.equal(s8 * 16, s4)
+    assert torch.equal(q8.to(torch.int16), 16 * q4.to(torch.int16) + residual.to(torch.int16))
+
+
+# --------------------------------------------------------------------------- GEMM vs goldens
+@pytest.mark.parametrize("w,a", PAIRS)
+@pytest.mark.parametrize("si", [0, 1, 2])
+def test_gemm_golden(ops, gemm_golden, w, a, si):
+    m, k, n = SHAPES[si]
+    key = f"s{si}_w{w}a{a}"
+    g = gemm_golden
+    pa = torch.from_numpy(g[f"{key}_pa"]).to(DEV)
+    as_ = torch.from_numpy(g[f"{key}_as"]).to(DEV)
+    pw = torch.from_numpy(g[f"{key}_pw"]).to(DEV)
+    ws = torch.from_numpy(g[f"{key}_ws"]).to(DEV)
+    bias = f32_of_bits(g[f"s{si}_bias"]).to(DEV)
+    for variant in (0, 1, 2, 3):
+        dots = ops.packed_linear_dots(pa, pw, k, w, a, variant=variant).cpu().numpy()
+        ref = g[f"{key}_dots"]
+        assert np.array_equal(dots[: ref.shape[0]], ref), f"dots variant {variant}"
+        y32 = ops.packed_linear(pa, as_, pw, ws, bias, k, w, a, out_dtype=torch.float32, variant=variant)
+        exact = O.packed_linear(g[f"{key}_pa"], g[f"{key}_as"], g[f"{key}_pw"], g[f"{key}_ws"],
+                                O.bf16_bits_to_f32(g[f"s{si}_bias"]), k, w, a, fma=True)
+        assert_bits(y32.cpu().numpy(), exact, f"fp32 output variant {variant}")
+        # Against the reference interpreter (no FMA): stated tolerance.
+        ref_y = g[f"{key}_y"]
+        rms = float(np.sqrt(np.mean(ref_y.astype(np.float64) ** 2)))
+        yb = ops.packed_linear(pa, as_, pw, ws, bias, k, w, a, out_dtype=torch.bfloat16, variant=variant)
+        assert float((yb.float().cpu() - torch.from_numpy(ref_y)).abs().max()) <= 1e-2 * rms + 1e-30
+
+
+# --------------------------------------------------------------------------- GEMM random / edge shapes
+def _case(ops, m, k, n, w, a, seed, bias_dtype=torch.bfloat16, out_dtype=torch.bfloat16, variant=0, rows=None):
+    x = inputs(m, k, seed)
+    wt = weight(n, k, seed)
+    codes, ws = ops.weight_codes(wt.to(DEV), w, a)
+    pw = ops.pack_rows(codes, w)
+    pa, as_ = ops.quantize_group64(x.to(DEV), a)
+    bias = None if bias_dtype is None else (torch.randn(n, generator=torch.Generator().manual_seed(seed)) * 0.1).to(
+        bias_dtype)
+    y = ops.packed_linear(pa, as_, pw, ws, None if bias is None else bias.to(DEV), k, w, a, out_dtype=out_dtype,
+                          variant=variant)
+    sel = np.arange(m) if rows is None else np.asarray(rows)
+    pa_h, as_h = pa.cpu().numpy()[sel], as_.cpu().numpy()[sel]
+    ref = O.packed_linear(pa_h, as_h, pw.cpu().numpy(), ws.cpu().numpy(),
+                          None if bias is None else bias.float().numpy(), k, w, a, fma=True)
+    return y.cpu()[torch.from_numpy(sel)], ref, (pa, pw, pa_h)
+
+
+@pytest.mark.parametrize("w,a", PAIRS)
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 4096), (8, 4096, 12288), (130, 1024, 200), (300, 192, 136)])
+def test_gemm_random_bit_exact(ops, w, a, m, k, n):
+    y, ref, _ = _case(ops, m, k, n, w, a, seed=m + k + n + 10 * w + a)
+    assert_bits(bf16_bits(y), O.to_bf16_bits(ref), "bf16 output")
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("bias_dtype", [None, torch.float32, torch.float16, torch.bfloat16])
+def test_gemm_dtypes(ops, out_dtype, bias_dtype):
+    y, ref, _ = _case(ops, 70, 384, 100, 4, 8, seed=5, bias_dtype=bias_dtype, out_dtype=out_dtype)
+    if out_dtype == torch.float32:
+        assert_bits(y.numpy(), ref, "fp32 output")
+    elif out_dtype == torch.bfloat16:
+        assert_bits(bf16_bits(y), O.to_bf16_bits(ref), "bf16 output")
+    else:
+        assert torch.equal(y, torch.from_numpy(ref).half())
+
+
+@pytest.mark.parametrize("w,a", [(4, 8), (4, 4), (2, 2), (8, 8)])
+def test_gemm_llama_shapes_row_sample(ops, w, a):
+    """Config-1 shapes at M=512: 8 sampled rows against the oracle (rows are independent)."""
+    rows = [0, 1, 127, 128, 255, 300, 510, 511]
+    for k, n in [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]:
+        y, ref, _ = _case(ops, 512, k, n, w, a, seed=k + n, rows=rows)
+        assert_bits(bf16_bits(y), O.to_bf16_bits(ref), f"bf16 output K={k} N={n}")
+
+
+def test_gemm_dots_full_size_properties(ops):
+    """Full-size W4A8 QKV: the per-group dots equal the oracle on sampled rows and
+    are invariant to the tile variant."""
+    m, k, n, w, a = 600, 4096, 12288, 4, 8
+    x = inputs(m, k, 11)
+    codes, ws = ops.weight_codes(weight(n, k, 11).to(DEV), w, a)
+    pw = ops.pack_rows(codes, w)
+    pa, as_ = ops.quantize_group64(x.to(DEV), a)
+    d0 = ops.packed_linear_dots(pa, pw, k, w, a, variant=3)
+    d1 = ops.packed_linear_dots(pa, pw, k, w, a, variant=1)
+    assert torch.equal(d0, d1)
+    rows = [0, 99, 511, 599]
+    ref = O.group_dots(pa.cpu().numpy()[rows], pw.cpu().numpy(), k, w, a)
+    assert np.array_equal(d0.cpu().numpy()[rows], ref)
+
+
+def test_gemm_empty(ops):
+    pa = torch.empty(0, 64, device=DEV, dtype=torch.uint8)
+    as_ = torch.empty(0, 1, device=DEV, dtype=torch.float32)
+    pw = torch.zeros(32, 32, device=DEV, dtype=torch.uint8)
+    ws = torch.ones(32, device=DEV)
+    y = ops.packed_linear(pa, as_, pw, ws, None, 64, 4, 8)
+    assert y.shape == (0, 32)
+
+
+def test_gemm_rejects_bad_arguments(ops):
+    from actune_b200._lib import ActuneError
+    pa = torch.zeros(4, 64, device=DEV, dtype=torch.uint8)
+    as_ = torch.ones(4, 1, device=DEV)
+    pw = torch.zeros(32, 32, device=DEV, dtype=torch.uint8)
+    ws = torch.ones(32, device=DEV)
+    with pytest.raises(RuntimeError):
+        ops.packed_linear(pa, as_, pw, ws, None, 64, 3, 8)      # W outside {2,4,8}
+    with pytest.raises(RuntimeError):
+        ops.packed_linear(pa, as_, pw, ws, None, 63, 4, 8)      # K not a multiple of 64
+    shifted = torch.zeros(4 * 64 + 1, device=DEV, dtype=torch.uint8)[1:].view(4, 64)
+    with pytest.raises(ActuneError) as err:
+        ops.packed_linear(shifted, as_, pw, ws, None, 64, 4, 8)  # TMA needs 16-byte alignment
+    assert err.value.status == 2
