@@ -21,6 +21,9 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 BUILD = PKG / "_build"
 LIB = PKG / "libactune_b200.so"
+# Optional extra nvcc defines and output path, for building experimental
+# variants side by side (e.g. ACTUNE_B200_DEFINES="-DACTUNE_PREBIAS=1").
+EXTRA_DEFINES = os.environ.get("ACTUNE_B200_DEFINES", "").split()
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-rdc=true", "-Xcompiler", "-fPIC,-O2",
@@ -45,17 +48,20 @@ def _stale(target: Path, deps) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build(force: bool = False, verbose_ptxas: bool = False, jobs: int | None = None) -> Path:
+def build(force: bool = False, verbose_ptxas: bool = False, jobs: int | None = None,
+          out: Path | None = None) -> Path:
     headers = list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
     srcs = sources()
-    BUILD.mkdir(exist_ok=True)
-    objs = [BUILD / (s.stem + ".o") for s in srcs]
+    lib = Path(out) if out else LIB
+    build_dir = BUILD if out is None else lib.parent / ("_build_" + lib.stem)
+    build_dir.mkdir(exist_ok=True, parents=True)
+    objs = [build_dir / (s.stem + ".o") for s in srcs]
     todo = [(s, o) for s, o in zip(srcs, objs) if force or _stale(o, [s, *headers, Path(__file__)])]
     cc = nvcc()
 
     def compile_one(so):
         s, o = so
-        cmd = [cc, *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(s), "-o", str(o)]
+        cmd = [cc, *ARCH, *NVCC_FLAGS, *EXTRA_DEFINES, "-I", str(INCLUDE), "-c", str(s), "-o", str(o)]
         if verbose_ptxas:
             cmd += ["-Xptxas", "-v"]
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -68,14 +74,13 @@ def build(force: bool = False, verbose_ptxas: bool = False, jobs: int | None = N
             for name, err in ex.map(compile_one, todo):
                 if verbose_ptxas and err:
                     print(f"== {name}\n{err}")
-    if force or todo or _stale(LIB, objs):
-        cmd = [cc, *ARCH, "-shared", "-rdc=true", "-cudart", "static", "-o", str(LIB), *map(str, objs),
-               "-Xcompiler", "-fPIC", "-lcuda" if False else ""]
-        cmd = [c for c in cmd if c]
+    if force or todo or _stale(lib, objs):
+        cmd = [cc, *ARCH, "-shared", "-rdc=true", "-cudart", "static", "-o", str(lib), *map(str, objs),
+               "-Xcompiler", "-fPIC"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc link failed:\n{r.stdout}\n{r.stderr}")
-    return LIB
+    return lib
 
 
 def main():
@@ -83,8 +88,9 @@ def main():
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose-ptxas", action="store_true")
     ap.add_argument("--jobs", type=int, default=None)
+    ap.add_argument("--out", default=None, help="output library path (default: in-tree libactune_b200.so)")
     a = ap.parse_args()
-    print(build(force=a.force, verbose_ptxas=a.verbose_ptxas, jobs=a.jobs))
+    print(build(force=a.force, verbose_ptxas=a.verbose_ptxas, jobs=a.jobs, out=a.out))
 
 
 if __name__ == "__main__":

@@ -8,7 +8,7 @@
 #include <atomic>
 #include <mutex>
 
-#include "../../include/actune_b200.h"
+#include "actune_b200.h"
 #include "kernels.cuh"
 
 namespace actune {
@@ -83,15 +83,16 @@ int pick_bn(int variant, int64_t M, int64_t N, int num_sms) {
     case ACTUNE_VARIANT_BN128: return 128;
     default: break;
   }
-  // Minimise waves x tile width (time per tile grows with BN); prefer wider
-  // tiles on ties (fewer re-reads of the activation tile).
+  // Minimise waves x per-tile time, modelled as (BN + 64) (a tile has a fixed
+  // cost for its 128-row activation stream and epilogue besides its BN weight
+  // rows); prefer wider tiles on ties.
   const int64_t mt = (M + 127) / 128;
   int best = 128;
   int64_t best_cost = INT64_MAX;
   for (int bn : {128, 64, 32}) {
     const int64_t tiles = mt * ((N + bn - 1) / bn);
     const int64_t waves = (tiles + num_sms - 1) / num_sms;
-    const int64_t cost = waves * bn;
+    const int64_t cost = waves * (bn + 64);
     if (cost < best_cost) {
       best_cost = cost;
       best = bn;

@@ -74,16 +74,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes (woken by the barrier) or about `hint_ns` elapse, instead of
+// spinning and taking issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms per sleep; the 2 s limit is checked between sleeps
+
 // Wait for the phase with the given parity to complete; false after the limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (true) {
-    if (mbar_try_wait(addr, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) {
-      report_error(1 /* ACTUNE_DEV_TIMEOUT */, site);
-      return false;
+  uint64_t t0 = 0;
+  for (uint32_t spin = 0;; ++spin) {
+    if (mbar_try_wait_sleep(addr, parity, kSuspendHintNs)) return true;
+    if ((spin & 15) == 15) {
+      const uint64_t now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        report_error(1 /* ACTUNE_DEV_TIMEOUT */, site);
+        return false;
+      }
     }
   }
 }
@@ -149,6 +171,42 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Store one 32-bit value to 32 lanes x N columns (N = 8, 16 or 32).
+template <int N>
+__device__ __forceinline__ void tmem_fill(uint32_t taddr, uint32_t v) {
+  if constexpr (N == 32) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+        "r"(v)
+        : "memory");
+  } else if constexpr (N == 16) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(
+                     taddr),
+                 "r"(v)
+                 : "memory");
+  } else {
+    static_assert(N == 8, "tmem_fill width");
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v)
+                 : "memory");
+  }
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 4 columns of 32-bit -> 4 registers per thread.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+
+// 32 lanes x 8 columns of 32-bit -> 8 registers per thread.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
 // 32 lanes x 16 columns of 32-bit -> 16 registers per thread.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -193,25 +251,8 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
 // ---------------------------------------------------------------------------
 // Packed fp32x2 arithmetic (sm_100): two lanes of IEEE binary32, RNE, one issue.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
-
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // Exact int32 -> fp32 for |v| < 2^22: the bit pattern 0x4B400000 + v is the
 // binary32 number 1.5*2^23 + v (ulp 1 in that binade); subtracting 1.5*2^23

@@ -9,17 +9,17 @@
 // y = fma(acc, ws[n], bias[n]) (or acc * ws[n] without bias), rounded once to
 // the output type.  Every W x A pair in {2,4,8}^2 runs on tcgen05 kind::i8.
 //
-// CTA tile: 128 token rows (TMEM lanes) x BN weight rows (TMEM columns);
-// K is streamed in stages of 128 (two groups of 64).  Warp roles:
+// CTA tile: 128 token rows (TMEM lanes) x BN weight rows (TMEM columns); K is
+// streamed in stages of 128 = two groups of 64.  Each stage's two groups go to
+// a pair of TMEM int32 accumulator buffers (NPAIR pairs rotate), so the MMA
+// issuer and the epilogue hand off once per stage.  Warp roles:
 //   warp 0      TMA producer: packed activation and weight tiles -> smem ring
-//   warp 1      TMEM owner + single-thread tcgen05.mma issuer; each 64-wide
-//               group goes into its own TMEM int32 accumulator buffer
-//               (NACC buffers rotate so the epilogue of group g overlaps the
-//               MMAs of groups g+1..)
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer (straight-line
+//               4 MMAs per stage from precomputed descriptors)
 //   warps 2-3   converters: sub-byte codes -> int8 in the canonical
 //               128B-swizzled K-major layout (code placed in the top bits of
 //               the byte, i.e. scaled by 2^(8-bits); compensated exactly in fp32)
-//   warps 4..   epilogue: tcgen05.ld of each group's int32 dots, exact
+//   warps 4-11  epilogue: tcgen05.ld of each group's int32 dots, exact
 //               int->fp32 conversion, packed fp32x2 FMA into register
 //               accumulators, final scale/bias/convert/store
 #pragma once
@@ -52,11 +52,11 @@ struct Group64Cfg {
   static_assert(BN == 32 || BN == 64 || BN == 128, "BN");
   static constexpr int BM = 128;     // token rows per tile = TMEM lanes = MMA M
   static constexpr int KS = 128;     // K elements per pipeline stage (two groups)
-  static constexpr int EPI_WG = 2;                // two epilogue warpgroups split the columns
+  static constexpr int EPI_WG = 2;   // two epilogue warpgroups split the columns
   static constexpr int COLS = BN / EPI_WG;      // accumulator columns per epilogue thread
   static constexpr int THREADS = 128 + 128 * EPI_WG;
-  static constexpr int NACC = BN == 32 ? 8 : 4;    // TMEM int32 accumulator buffers
-  static constexpr int TMEM_COLS = NACC * BN;      // 256 or 512 (power of two)
+  static constexpr int NPAIR = BN == 32 ? 4 : 2;   // accumulator buffer pairs (one pair per stage)
+  static constexpr int TMEM_COLS = NPAIR * 2 * BN; // 256 or 512 (power of two)
   static constexpr bool CONVERT = (A < 8) || (W < 8);
   // Per-stage shared-memory layout: [act int8 | wgt int8 | act packed | wgt packed].
   static constexpr int OP_A_BYTES = BM * KS;        // 16 KB, SW128 K-major
@@ -77,23 +77,32 @@ struct Group64Cfg {
 
 // Unpack one stage of packed sub-byte codes (ROWS rows x 128 codes, row pitch
 // 16*BITS bytes) into the SW128 K-major int8 operand (row pitch 128 bytes,
-// 16-byte chunk c of row r stored at chunk c ^ (r mod 8)).
+// 16-byte chunk c of row r stored at chunk c ^ (r mod 8)).  One item = 16
+// packed bytes = 2 (BITS 4) or 4 (BITS 2) output chunks.
 template <int BITS, int ROWS>
 __device__ __forceinline__ void unpack_stage(const uint8_t* __restrict__ stg, uint8_t* __restrict__ op, int tid,
                                              int nthreads) {
-#pragma unroll 4
-  for (int item = tid; item < ROWS * 8; item += nthreads) {
-    const int r = item >> 3, c = item & 7;
-    uint4 v;
+  constexpr int ITEMS_PER_ROW = BITS;       // 16*BITS packed bytes per row / 16
+  constexpr int CHUNKS = 8 / ITEMS_PER_ROW;  // output chunks per item
+#pragma unroll 2
+  for (int item = tid; item < ROWS * ITEMS_PER_ROW; item += nthreads) {
+    const int r = item / ITEMS_PER_ROW, i = item % ITEMS_PER_ROW;
+    const uint4 src = *reinterpret_cast<const uint4*>(stg + item * 16);
+    uint8_t* row = op + (r >> 3) * 1024 + (r & 7) * 128;
+    const int x = r & 7;
+    const int c0 = i * CHUNKS;
     if constexpr (BITS == 4) {
-      const uint2 src = *reinterpret_cast<const uint2*>(stg + r * 64 + c * 8);
-      const uint2 lo = unpack_w4_word(src.x), hi = unpack_w4_word(src.y);
-      v = make_uint4(lo.x, lo.y, hi.x, hi.y);
+      const uint2 a = unpack_w4_word(src.x), b = unpack_w4_word(src.y);
+      const uint2 c = unpack_w4_word(src.z), d = unpack_w4_word(src.w);
+      *reinterpret_cast<uint4*>(row + (((c0 + 0) ^ x) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
+      *reinterpret_cast<uint4*>(row + (((c0 + 1) ^ x) << 4)) = make_uint4(c.x, c.y, d.x, d.y);
     } else {
-      const uint32_t src = *reinterpret_cast<const uint32_t*>(stg + r * 32 + c * 4);
-      v = unpack_w2_word(src);
+      static_assert(BITS == 2, "BITS");
+      *reinterpret_cast<uint4*>(row + (((c0 + 0) ^ x) << 4)) = unpack_w2_word(src.x);
+      *reinterpret_cast<uint4*>(row + (((c0 + 1) ^ x) << 4)) = unpack_w2_word(src.y);
+      *reinterpret_cast<uint4*>(row + (((c0 + 2) ^ x) << 4)) = unpack_w2_word(src.z);
+      *reinterpret_cast<uint4*>(row + (((c0 + 3) ^ x) << 4)) = unpack_w2_word(src.w);
     }
-    *reinterpret_cast<uint4*>(op + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) = v;
   }
 }
 
@@ -115,7 +124,45 @@ __device__ __forceinline__ void store_scalar(const GemmParams& p, int64_t idx, f
   else reinterpret_cast<float*>(p.out)[idx] = y;
 }
 
-template <int W, int A, int BN>
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
+  if constexpr (N == 32) {
+    tmem_ld32(taddr, r);
+  } else if constexpr (N == 16) {
+    tmem_ld16(taddr, r);
+  } else if constexpr (N == 8) {
+    tmem_ld8(taddr, r);
+  } else {
+    static_assert(N == 4, "tmem_ld width");
+    tmem_ld4(taddr, r);
+  }
+}
+
+// acc[j] += float(d[2j..2j+1]) * s for H int32 dots (exact conversion, packed fp32x2 FMA).
+template <int H>
+__device__ __forceinline__ void accumulate(float2* acc, const uint32_t (&d)[H], float s) {
+  const float2 s2 = make_float2(s, s);
+  const float2 magic = make_float2(-kMagicValue, -kMagicValue);
+#pragma unroll
+  for (int j = 0; j < H / 2; ++j) {
+    float2 f = make_float2(__uint_as_float(d[2 * j] + kMagicBits), __uint_as_float(d[2 * j + 1] + kMagicBits));
+    f = fadd2(f, magic);
+    acc[j] = ffma2(f, s2, acc[j]);
+  }
+}
+
+template <int H>
+__device__ __forceinline__ void store_dots(const GemmParams& p, int m, int col, int g, const uint32_t (&d)[H],
+                                           int shift) {
+  if (m >= p.M) return;
+#pragma unroll
+  for (int j = 0; j < H; ++j) {
+    const int n = col + j;
+    if (n < p.N) p.dots[((int64_t)m * p.N + n) * p.G + g] = static_cast<int32_t>(d[j]) >> shift;
+  }
+}
+
+template <int W, int A, int BN, bool DOTS>
 __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
     group64_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
                         const GemmParams p) {
@@ -124,8 +171,8 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
   __shared__ __align__(8) uint64_t full_raw[C::STAGES];
   __shared__ __align__(8) uint64_t full_op[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
-  __shared__ __align__(8) uint64_t acc_full[C::NACC];
-  __shared__ __align__(8) uint64_t acc_empty[C::NACC];
+  __shared__ __align__(8) uint64_t acc_full[C::NPAIR];
+  __shared__ __align__(8) uint64_t acc_empty[C::NPAIR];
   __shared__ __align__(8) uint64_t mma_done;
   __shared__ uint32_t tmem_holder;
 
@@ -142,7 +189,7 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
       mbar_init(&full_op[s], 2);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int b = 0; b < C::NACC; ++b) {
+    for (int b = 0; b < C::NPAIR; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4 * C::EPI_WG);
     }
@@ -183,33 +230,32 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Straight-line per stage: wait operands, wait the accumulator pair,
+    // 4 MMAs, 2 commits.  Descriptors differ only in their start-address field
+    // (16-byte units): +2 per 32-byte K step, +STAGE_BYTES/16 per stage.
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_i8(C::BM, BN);
-      int g = 0;
-      bool ok = true;
-      for (int it = 0; it < n_iters && ok; ++it) {
+      const uint64_t desc_a0 = smem_desc_sw128(smem_u32(smem));
+      const uint64_t desc_w0 = smem_desc_sw128(smem_u32(smem) + C::OP_A_BYTES);
+      constexpr uint64_t kStageStep = (uint64_t)(C::STAGE_BYTES >> 4);
+      for (int it = 0; it < n_iters; ++it) {
         const int s = it % C::STAGES;
+        const int pr = it % C::NPAIR;
         uint64_t* ready = C::CONVERT ? &full_op[s] : &full_raw[s];
         if (!mbar_wait(ready, (it / C::STAGES) & 1, kSiteMmaFull)) break;
+        if (!mbar_wait(&acc_empty[pr], ((it / C::NPAIR) & 1) ^ 1, kSiteMmaAcc)) break;
         tc_fence_after();
-        const uint32_t op_a = smem_u32(smem + s * C::STAGE_BYTES);
-        const uint32_t op_w = op_a + C::OP_A_BYTES;
-        for (int gi = 0; gi < 2 && g < G; ++gi, ++g) {
-          const int b = g % C::NACC;
-          if (!mbar_wait(&acc_empty[b], ((g / C::NACC) & 1) ^ 1, kSiteMmaAcc)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem_base + b * BN;
-#pragma unroll
-          for (int kk = 0; kk < 2; ++kk) {
-            const uint32_t koff = gi * 64 + kk * 32;
-            mma_i8(d, smem_desc_sw128(op_a + koff), smem_desc_sw128(op_w + koff), idesc, kk);
-          }
-          mma_commit(&acc_full[b]);
+        const uint64_t da = desc_a0 + kStageStep * s;
+        const uint64_t dw = desc_w0 + kStageStep * s;
+        const uint32_t d0 = tmem_base + pr * (2 * BN);
+        mma_i8(d0, da + 0, dw + 0, idesc, 0u);  // group 2it:   K bytes 0..31
+        mma_i8(d0, da + 2, dw + 2, idesc, 1u);  //              K bytes 32..63
+        if (2 * it + 1 < G) {
+          mma_i8(d0 + BN, da + 4, dw + 4, idesc, 0u);  // group 2it+1: K bytes 64..95
+          mma_i8(d0 + BN, da + 6, dw + 6, idesc, 1u);  //              K bytes 96..127
         }
-        if (ok) mma_commit(&empty_bar[s]);
+        mma_commit(&acc_full[pr]);
+        mma_commit(&empty_bar[s]);
       }
       mma_commit(&mma_done);
       mbar_wait(&mma_done, 0, kSiteMmaDone);
@@ -232,6 +278,11 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each thread owns one token row (TMEM lane) and COLS columns, read from
+    // TMEM in halves of H columns.  Within a stage each half-load overlaps the
+    // accumulation of the previous half, and the first half of the next stage
+    // is loaded before the last half of this one is accumulated.  Activation
+    // scales are fetched two stages ahead into static register slots.
     const int ew = warp - 4;
     const int q = ew & 3;        // TMEM lane quarter this warp may access
     const int e = ew >> 2;       // column slice
@@ -239,72 +290,100 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
     const int m = m0 + row;
     const bool warp_live = (m0 + q * 32) < p.M;  // any valid token row in this warp
     const int col0 = n0 + e * C::COLS;
+    constexpr int H = C::COLS / 2;
     const float shift_scale = 1.0f / float(1 << C::SHIFT);
+    const bool load_scales = !DOTS && warp_live && m < p.M;
     const float* as_row = p.act_scale + (int64_t)(m < p.M ? m : 0) * G;
-    (void)col0;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + e * C::COLS;
     float2 acc[C::COLS / 2];
 #pragma unroll
     for (int j = 0; j < C::COLS / 2; ++j) acc[j] = make_float2(0.f, 0.f);
-    const bool load_scales = warp_live && m < p.M && p.dots == nullptr;
-    float s_next = load_scales ? __ldg(as_row) : 0.f;
+    auto scale_at = [&](int g) -> float { return (load_scales && g < G) ? __ldg(as_row + g) : 0.f; };
+    uint32_t ra[H], rb[H];
     bool ok = true;
-    for (int g = 0; g < G; ++g) {
-      const int b = g % C::NACC;
-      const float s_cur = s_next * shift_scale;
-      if (g + 1 < G) s_next = load_scales ? __ldg(as_row + g + 1) : 0.f;
-      if (!mbar_wait(&acc_full[b], (g / C::NACC) & 1, kSiteEpilogue)) {
-        ok = false;
-        break;
+    if (!warp_live) {
+      // No valid token row in this warp: only keep the accumulator handshake.
+      for (int it = 0; it < n_iters; ++it) {
+        const int pr = it % C::NPAIR;
+        if (!mbar_wait(&acc_full[pr], (it / C::NPAIR) & 1, kSiteEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[pr]);
       }
-      tc_fence_after();
-      if (warp_live) {
-        uint32_t r[C::COLS];
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + b * BN + e * C::COLS;
-        if constexpr (C::COLS % 32 == 0) {
-#pragma unroll
-          for (int c = 0; c < C::COLS; c += 32) tmem_ld32(taddr + c, *reinterpret_cast<uint32_t(*)[32]>(&r[c]));
-        } else {
-#pragma unroll
-          for (int c = 0; c < C::COLS; c += 16) tmem_ld16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(&r[c]));
-        }
+    } else {
+      ok = mbar_wait(&acc_full[0], 0, kSiteEpilogue);
+      if (ok) {
+        tc_fence_after();
+        tmem_ld<H>(lane_base, ra);
         tmem_wait_ld();
+      }
+      // One stage: ra already holds (group 2it, first half).
+      auto stage = [&](int it, float s0raw, float s1raw) {
+        const int pr = it % C::NPAIR;
+        const uint32_t base = lane_base + pr * (2 * BN);
+        const int g0 = 2 * it;
+        const bool second = g0 + 1 < G;
+        const float s0 = s0raw * shift_scale, s1 = s1raw * shift_scale;
+        tmem_ld<H>(base + H, rb);
+        if constexpr (DOTS) store_dots<H>(p, m, col0, g0, ra, C::SHIFT);
+        else accumulate<H>(acc, ra, s0);
+        tmem_wait_ld();
+        if (second) {
+          tmem_ld<H>(base + BN, ra);
+          if constexpr (DOTS) store_dots<H>(p, m, col0 + H, g0, rb, C::SHIFT);
+          else accumulate<H>(acc + H / 2, rb, s0);
+          tmem_wait_ld();
+          tmem_ld<H>(base + BN + H, rb);
+          if constexpr (DOTS) store_dots<H>(p, m, col0, g0 + 1, ra, C::SHIFT);
+          else accumulate<H>(acc, ra, s1);
+          tmem_wait_ld();
+        }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[b]);
-        if (p.dots != nullptr) {
-          if (m < p.M) {
-#pragma unroll
-            for (int j = 0; j < C::COLS; ++j) {
-              const int n = col0 + j;
-              if (n < p.N) p.dots[((int64_t)m * p.N + n) * G + g] = static_cast<int32_t>(r[j]) >> C::SHIFT;
-            }
-          }
-        } else {
-          const float2 s2 = make_float2(s_cur, s_cur);
-          const float2 magic = make_float2(-kMagicValue, -kMagicValue);
-#pragma unroll
-          for (int j = 0; j < C::COLS / 2; ++j) {
-            float2 f = make_float2(__uint_as_float(r[2 * j] + kMagicBits), __uint_as_float(r[2 * j + 1] + kMagicBits));
-            f = fadd2(f, magic);
-            acc[j] = ffma2(f, s2, acc[j]);
+        if (lane == 0) mbar_arrive(&acc_empty[pr]);
+        if (it + 1 < n_iters) {
+          const int pn = (it + 1) % C::NPAIR;
+          if (!mbar_wait(&acc_full[pn], ((it + 1) / C::NPAIR) & 1, kSiteEpilogue)) {
+            ok = false;
+          } else {
+            tc_fence_after();
+            tmem_ld<H>(lane_base + pn * (2 * BN), ra);
           }
         }
-      } else {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[b]);
+        if constexpr (DOTS) store_dots<H>(p, m, col0 + H, second ? g0 + 1 : g0, rb, C::SHIFT);
+        else accumulate<H>(acc + H / 2, rb, second ? s1 : s0);
+        tmem_wait_ld();
+      };
+      // Scale slots: x for even stages, y for odd stages (fetched two stages ahead).
+      float x0 = scale_at(0), x1 = scale_at(1), y0 = scale_at(2), y1 = scale_at(3);
+      for (int it = 0; it < n_iters && ok; it += 2) {
+        const float a0 = x0, a1 = x1;
+        x0 = scale_at(2 * it + 4);
+        x1 = scale_at(2 * it + 5);
+        stage(it, a0, a1);
+        if (it + 1 < n_iters && ok) {
+          const float b0 = y0, b1 = y1;
+          y0 = scale_at(2 * it + 6);
+          y1 = scale_at(2 * it + 7);
+          stage(it + 1, b0, b1);
+        }
       }
     }
+
     // Final epilogue: stage fp32 accumulators through the (now idle) pipeline
     // shared memory, then every epilogue thread applies ws/bias to 8
     // consecutive columns of one row and writes them with one coalesced store.
-    if (p.dots == nullptr) {
+    if constexpr (!DOTS) {
       constexpr int LD = BN + 4;  // padded row pitch (floats)
-      float* stage = reinterpret_cast<float*>(smem);
+      float* stage_buf = reinterpret_cast<float*>(smem);
       if (ok) {
 #pragma unroll
         for (int j = 0; j < C::COLS / 2; ++j)
-          *reinterpret_cast<float2*>(stage + row * LD + e * C::COLS + 2 * j) = acc[j];
+          *reinterpret_cast<float2*>(stage_buf + row * LD + e * C::COLS + 2 * j) = acc[j];
       }
       named_barrier_sync(1, 128 * C::EPI_WG);
       if (ok) {
@@ -314,8 +393,8 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
           const int r = chunk / (BN / 8), c8 = (chunk % (BN / 8)) * 8;
           const int n = n0 + c8;
           if (n >= p.N) continue;
-          const float4 lo = *reinterpret_cast<const float4*>(stage + r * LD + c8);
-          const float4 hi = *reinterpret_cast<const float4*>(stage + r * LD + c8 + 4);
+          const float4 lo = *reinterpret_cast<const float4*>(stage_buf + r * LD + c8);
+          const float4 hi = *reinterpret_cast<const float4*>(stage_buf + r * LD + c8 + 4);
           const float a8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
           const int64_t orow = (int64_t)(m0 + r) * p.N;
           if (p.out_vec_ok && n + 8 <= p.N && p.out_dtype != kDtF32) {

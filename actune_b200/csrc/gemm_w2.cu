@@ -7,15 +7,16 @@ template <int W, int A, int BN>
 cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
                                 cudaStream_t stream) {
   using C = Group64Cfg<W, A, BN>;
-  auto kernel = group64_gemm_kernel<W, A, BN>;
+  const bool dots = p.dots != nullptr;
+  auto kernel = dots ? group64_gemm_kernel<W, A, BN, true> : group64_gemm_kernel<W, A, BN, false>;
   int dev = 0;
   cudaGetDevice(&dev);
-  static bool configured[64] = {};
+  static bool configured[2][64] = {};
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
+  if (!configured[dots][dev]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    configured[dots][dev] = true;
   }
   const dim3 grid((p.M + C::BM - 1) / C::BM, (p.N + BN - 1) / BN);
   kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);

@@ -147,11 +147,15 @@ def test_gemm_golden(ops, gemm_golden, w, a, si):
         exact = O.packed_linear(g[f"{key}_pa"], g[f"{key}_as"], g[f"{key}_pw"], g[f"{key}_ws"],
                                 O.bf16_bits_to_f32(g[f"s{si}_bias"]), k, w, a, fma=True)
         assert_bits(y32.cpu().numpy(), exact, f"fp32 output variant {variant}")
-        # Against the reference interpreter (no FMA): stated tolerance.
-        ref_y = g[f"{key}_y"]
-        rms = float(np.sqrt(np.mean(ref_y.astype(np.float64) ** 2)))
+        # Against the reference run under the Triton interpreter (separate
+        # multiply and add, no FMA), both rounded to bf16: the two evaluation
+        # modes of the reference itself may differ by one bf16 ulp where the
+        # fp32 values straddle a rounding boundary; nothing else may differ.
+        ref_bits = O.to_bf16_bits(g[f"{key}_y"])
         yb = ops.packed_linear(pa, as_, pw, ws, bias, k, w, a, out_dtype=torch.bfloat16, variant=variant)
-        assert float((yb.float().cpu() - torch.from_numpy(ref_y)).abs().max()) <= 1e-2 * rms + 1e-30
+        ours = bf16_bits(yb).astype(np.int32)
+        ulps = np.abs(ours - ref_bits.astype(np.int32))
+        assert ulps.max() <= 1 and (ulps > 0).mean() <= 0.01, f"{(ulps > 0).sum()} elements differ"
 
 
 # --------------------------------------------------------------------------- GEMM random / edge shapes
