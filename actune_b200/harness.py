@@ -1,0 +1,210 @@
+"""Benchmark backbones: an OpenVLA-OFT-shaped Llama-2-7B policy with a W4A8 bank.
+
+The reference runs its packed linears inside external OFT / OpenPI models
+(actune/models/oft.py, actune/models/pi05.py).  Those are not installable here,
+so the benchmark uses a random-init backbone of the same shape:
+
+* Llama-2-7B: 32 decoder layers, hidden 4096, 32 heads x 128, MLP 11008,
+  RMSNorm (eps 1e-5), rotary embedding, bf16; fused QKV (4096 -> 12288) and
+  fused gate/up (4096 -> 22016) projections, so the four packed linears per
+  layer have exactly the Llama-2-7B projection shapes;
+* a prefix of 512 vision + 32 prompt tokens followed by 8 x 7 = 56
+  parallel-decoded action tokens (600 tokens per call), whose final states go
+  through a small bf16 action head to an [8, 7] action chunk.
+
+Every projection is a bank target, installed with ``install_bank`` (so it runs
+the packed-integer path) under a W4A8-average ``SharedBank`` with two binary
+switchable matrices.  Attention uses torch SDPA; norms, rotary embedding and
+the gated activation use the glue kernels of include/actune_b200_harness.h.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from .layers import expected_version_bytes, install_bank
+from .precision import CONFIGURATIONS, SharedBank
+
+_H = None
+
+
+def _hlib():
+    global _H
+    if _H is None:
+        L = _lib.lib()
+        p, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+        L.actune_harness_rmsnorm.argtypes = [p, p, p, p, p, i64, i64, ctypes.c_float, i32, p]
+        L.actune_harness_rmsnorm.restype = i32
+        L.actune_harness_rope.argtypes = [p, p, p, i64, i32, i32, i32, p]
+        L.actune_harness_rope.restype = i32
+        L.actune_harness_gated_act.argtypes = [p, p, i64, i64, i32, p]
+        L.actune_harness_gated_act.restype = i32
+        _H = L
+    return _H
+
+
+def _p(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _s(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def rmsnorm(x, weight, eps, residual=None, gemma=False):
+    """(normed, new_residual): fused residual add + RMSNorm over the last dim."""
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    res_out = torch.empty_like(x) if residual is not None else None
+    T, D = x.numel() // x.shape[-1], x.shape[-1]
+    _lib.check(_hlib().actune_harness_rmsnorm(_p(x), _p(residual), _p(weight), _p(out), _p(res_out), T, D,
+                                               float(eps), 1 if gemma else 0, _s(x)), "rmsnorm")
+    return out, (res_out if residual is not None else x)
+
+
+def rope_(qkv, cos, sin, hq, hkv, dh):
+    T = qkv.numel() // qkv.shape[-1]
+    _lib.check(_hlib().actune_harness_rope(_p(qkv), _p(cos), _p(sin), T, hq, hkv, dh, _s(qkv)), "rope")
+    return qkv
+
+
+def gated_act(gu, gelu=False):
+    I = gu.shape[-1] // 2
+    T = gu.numel() // gu.shape[-1]
+    out = torch.empty(*gu.shape[:-1], I, device=gu.device, dtype=gu.dtype)
+    _lib.check(_hlib().actune_harness_gated_act(_p(gu.contiguous()), _p(out), T, I, 1 if gelu else 0, _s(gu)),
+               "gated_act")
+    return out
+
+
+def rope_tables(T, dh, theta, device):
+    inv = 1.0 / (theta ** (torch.arange(0, dh, 2, device=device, dtype=torch.float32) / dh))
+    ang = torch.arange(T, device=device, dtype=torch.float32)[:, None] * inv[None, :]
+    return ang.cos().contiguous(), ang.sin().contiguous()
+
+
+class DecoderLayer(torch.nn.Module):
+    """Pre-norm decoder layer with fused QKV and gate/up projections (Llama or Gemma flavour)."""
+
+    def __init__(self, hidden, heads, kv_heads, head_dim, mlp, eps, gemma, device, dtype):
+        super().__init__()
+        self.hidden, self.heads, self.kv_heads, self.head_dim, self.mlp = hidden, heads, kv_heads, head_dim, mlp
+        self.eps, self.gemma = eps, gemma
+        kw = dict(device=device, dtype=dtype)
+        self.input_norm = torch.nn.Parameter(torch.ones(hidden, **kw) if not gemma else torch.zeros(hidden, **kw))
+        self.post_norm = torch.nn.Parameter(torch.ones(hidden, **kw) if not gemma else torch.zeros(hidden, **kw))
+        self.qkv_proj = torch.nn.Linear(hidden, (heads + 2 * kv_heads) * head_dim, bias=False, **kw)
+        self.o_proj = torch.nn.Linear(heads * head_dim, hidden, bias=False, **kw)
+        self.gate_up_proj = torch.nn.Linear(hidden, 2 * mlp, bias=False, **kw)
+        self.down_proj = torch.nn.Linear(mlp, hidden, bias=False, **kw)
+
+    def forward(self, x, residual, cos, sin):
+        T = x.shape[0]
+        h, residual = rmsnorm(x, self.input_norm, self.eps, residual, self.gemma)
+        qkv = self.qkv_proj(h)
+        rope_(qkv, cos, sin, self.heads, self.kv_heads, self.head_dim)
+        q, k, v = qkv.split([self.heads * self.head_dim, self.kv_heads * self.head_dim,
+                             self.kv_heads * self.head_dim], dim=-1)
+        q = q.view(T, self.heads, self.head_dim).transpose(0, 1).unsqueeze(0)
+        k = k.view(T, self.kv_heads, self.head_dim).transpose(0, 1).unsqueeze(0)
+        v = v.view(T, self.kv_heads, self.head_dim).transpose(0, 1).unsqueeze(0)
+        attn = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=self.kv_heads != self.heads)
+        attn = attn.squeeze(0).transpose(0, 1).reshape(T, self.heads * self.head_dim)
+        x = self.o_proj(attn)
+        h, residual = rmsnorm(x, self.post_norm, self.eps, residual, self.gemma)
+        x = self.down_proj(gated_act(self.gate_up_proj(h), gelu=self.gemma))
+        return x, residual
+
+
+class OFTBackbone(torch.nn.Module):
+    """OpenVLA-OFT-shaped Llama-2-7B backbone + L1-regression-style action head."""
+
+    def __init__(self, layers=32, hidden=4096, heads=32, mlp=11008, tokens=600, action_tokens=56,
+                 chunk=(8, 7), device="cuda", dtype=torch.bfloat16, seed=0):
+        super().__init__()
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.tokens, self.action_tokens, self.chunk = tokens, action_tokens, chunk
+        self.layers = torch.nn.ModuleList(
+            [DecoderLayer(hidden, heads, heads, hidden // heads, mlp, 1e-5, False, device, dtype) for _ in range(layers)])
+        with torch.no_grad():
+            for layer in self.layers:
+                for lin in (layer.qkv_proj, layer.o_proj, layer.gate_up_proj, layer.down_proj):
+                    lin.weight.normal_(0.0, 0.02, generator=g)
+        self.final_norm = torch.nn.Parameter(torch.ones(hidden, device=device, dtype=dtype))
+        self.head1 = torch.nn.Linear(hidden, hidden, device=device, dtype=dtype)
+        self.head2 = torch.nn.Linear(hidden, 1, device=device, dtype=dtype)
+        with torch.no_grad():
+            for lin in (self.head1, self.head2):
+                lin.weight.normal_(0.0, 0.02, generator=g)
+                lin.bias.zero_()
+        cos, sin = rope_tables(tokens, hidden // heads, 10000.0, device)
+        self.register_buffer("rope_cos", cos)
+        self.register_buffer("rope_sin", sin)
+
+    def forward(self, embeds):
+        """embeds [tokens, hidden] bf16 -> actions [chunk] fp32."""
+        x, residual = embeds, None
+        for layer in self.layers:
+            x, residual = layer(x, residual, self.rope_cos, self.rope_sin)
+        h, _ = rmsnorm(x, self.final_norm, 1e-5, residual)
+        a = h[-self.action_tokens:]
+        a = self.head2(F.gelu(self.head1(a)))
+        return a.float().reshape(self.chunk)
+
+
+def projection_names(model):
+    names = []
+    for i in range(len(model.layers)):
+        for proj in ("qkv_proj", "o_proj", "gate_up_proj", "down_proj"):
+            names.append(f"layers.{i}.{proj}")
+    return names
+
+
+def build_w4a8_bank(model, tokens, switchable=("layers.0.down_proj", "layers.1.down_proj")):
+    """Synthetic W4A8-average SharedBank: every projection W4A8, two binary
+    switchable matrices (W4A8 / W2A8), four distinct configurations."""
+    names = projection_names(model)
+    shapes = {n: [model.get_submodule(n).out_features, model.get_submodule(n).in_features] for n in names}
+    counts = {n: tokens * shapes[n][1] for n in names}
+    base = {n: "w4a8" for n in names}
+    a, b = switchable
+    configurations = {
+        "q11": dict(base),
+        "q10": {**base, b: "w2a8"},
+        "q01": {**base, a: "w2a8"},
+        "q00": {**base, a: "w2a8", b: "w2a8"},
+    }
+    version_bytes = {n: {m: expected_version_bytes(shapes[n][0], shapes[n][1], int(m[1]), int(m[3]))
+                         for m in {c[n] for c in configurations.values()}} for n in names}
+    groups = {}
+    for n in names:
+        groups.setdefault(n.split(".")[-1], []).append(n)
+    resident = sum(version_bytes[n][m] for n in names for m in version_bytes[n])
+    bank = SharedBank(configurations=configurations, shapes=shapes, activation_elements=counts,
+                      shape_groups=list(groups.values()), version_bytes=version_bytes, budget="w4a8",
+                      storage_limit=resident + 1024)
+    clips = {n: {m: None for m in version_bytes[n]} for n in names}
+    return bank.validate(), clips
+
+
+def make_oft_policy(layers=32, tokens=600, device="cuda", seed=0):
+    """Build the backbone, install the packed bank (frees the bf16 weights) and
+    return (model, runtime)."""
+    model = OFTBackbone(layers=layers, tokens=tokens, device=device, seed=seed)
+    bank, clips = build_w4a8_bank(model, tokens)
+    runtime = install_bank(model, bank, clips)
+    torch.cuda.synchronize()
+    return model, runtime
+
+
+def config_cycle():
+    """Per-call precision order used by the benchmark: q00 -> q01 -> q11 -> q10."""
+    return ("q00", "q01", "q11", "q10")
+
+
+assert set(config_cycle()) == set(CONFIGURATIONS)
+_ = math  # keep import (rope tables use torch math)

@@ -1,0 +1,38 @@
+/*
+ * actune_b200 benchmark-harness kernels (bf16 glue around the packed linears of
+ * the Llama- and Gemma-shaped benchmark backbones).  Not part of the reference's
+ * packed-integer path; they replace the stock elementwise torch ops the
+ * reference's models run between projections (HF Llama/Gemma RMSNorm, rotary
+ * embedding, gated MLP activation) with one launch each.
+ * Same conventions as actune_b200.h: device pointers, caller-owned buffers,
+ * asynchronous on `stream`, actune_status return codes.
+ */
+#ifndef ACTUNE_B200_HARNESS_H
+#define ACTUNE_B200_HARNESS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Row-wise RMSNorm of x [T, D] bf16 (optionally after adding `residual`, whose
+ * sum is written to residual_out).  gemma != 0 selects the Gemma weight
+ * convention out = r * inv * (1 + w); otherwise out = w * bf16(r * inv). */
+int actune_harness_rmsnorm(const void* x, const void* residual, const void* weight, void* out, void* residual_out,
+                           int64_t T, int64_t D, float eps, int gemma, void* stream);
+
+/* In-place rotate-half rotary embedding of the q (Hq heads) and k (Hkv heads)
+ * parts of a fused bf16 [T, (Hq + 2*Hkv) * Dh] projection; cos/sin fp32 [T, Dh/2]. */
+int actune_harness_rope(void* qkv, const float* cos_t, const float* sin_t, int64_t T, int Hq, int Hkv, int Dh,
+                        void* stream);
+
+/* out [T, I] = act(gate) * up for gu [T, 2I] = [gate | up]; gelu != 0 uses
+ * tanh-GELU (Gemma), else SiLU (Llama). */
+int actune_harness_gated_act(const void* gu, void* out, int64_t T, int64_t I, int gelu, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ACTUNE_B200_HARNESS_H */
