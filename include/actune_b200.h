@@ -3,9 +3,10 @@
  *
  * Plain pointers and sizes only.  Every pointer argument is a device pointer on
  * the CUDA device that is current on the calling thread, unless noted.  The
- * caller owns every buffer; no function allocates device memory, so every call
- * can be captured into a CUDA graph (the first call of each kernel on a device
- * also sets its shared-memory attribute, so make one call before capturing).
+ * caller owns every buffer; no function allocates device memory.  The functions
+ * other than actune_grouped_linear_noalloc can be captured into a CUDA graph
+ * (the first call of each kernel on a device also sets its shared-memory
+ * attribute, so make one call before capturing).
  * `stream` is a cudaStream_t (NULL = legacy default stream).  All functions are
  * asynchronous with respect to the host and return an actune_status; a kernel
  * that fails on the device records the failure in a device word read by
@@ -117,6 +118,27 @@ size_t actune_grouped_linear_workspace_size(int64_t M, int64_t K, int A);
 int actune_grouped_linear(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* w, const float* w_scale,
                           const void* bias, int bias_dtype, int64_t N, int W, int A, void* out, int out_dtype,
                           void* workspace, size_t workspace_bytes, int variant, void* stream);
+
+/* Bytes of the fixed device scratch used by actune_grouped_linear_noalloc. */
+#define ACTUNE_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* actune_grouped_linear for callers that cannot allocate device memory (no
+ * counterpart in the reference; its GroupedLinear.forward allocates its
+ * temporaries with torch).  Hosts whose device memory is owned by another
+ * allocator, or loops that must not allocate once running, pass only inputs and
+ * outputs: the packed activations and scales live in a fixed array of
+ * ACTUNE_NOALLOC_SCRATCH_BYTES (8 MiB) in this library's device memory, held on
+ * every device that loads the library until the process exits.  Requests with
+ * actune_grouped_linear_workspace_size(M, K, A) above that size return
+ * ACTUNE_ERR_WORKSPACE without launching.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture.  The function allocates
+ * nothing.  All calls share the one array and it keeps the last call's contents
+ * (no part of it needs to start at zero): calls that overlap on the GPU (other
+ * streams, other threads) race on it and must be serialised by the caller. */
+int actune_grouped_linear_noalloc(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* w,
+                                  const float* w_scale, const void* bias, int bias_dtype, int64_t N, int W, int A,
+                                  void* out, int out_dtype, int variant, void* stream);
 
 /* Human-readable text for an actune_status (static storage). */
 const char* actune_status_string(int status);
