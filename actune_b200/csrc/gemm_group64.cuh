@@ -78,30 +78,38 @@ struct Group64Cfg {
 // Unpack one stage of packed sub-byte codes (ROWS rows x 128 codes, row pitch
 // 16*BITS bytes) into the SW128 K-major int8 operand (row pitch 128 bytes,
 // 16-byte chunk c of row r stored at chunk c ^ (r mod 8)).  One item = 16
-// packed bytes = 2 (BITS 4) or 4 (BITS 2) output chunks.
-template <int BITS, int ROWS>
-__device__ __forceinline__ void unpack_stage(const uint8_t* __restrict__ stg, uint8_t* __restrict__ op, int tid,
-                                             int nthreads) {
-  constexpr int ITEMS_PER_ROW = BITS;       // 16*BITS packed bytes per row / 16
-  constexpr int CHUNKS = 8 / ITEMS_PER_ROW;  // output chunks per item
-#pragma unroll 2
-  for (int item = tid; item < ROWS * ITEMS_PER_ROW; item += nthreads) {
-    const int r = item / ITEMS_PER_ROW, i = item % ITEMS_PER_ROW;
-    const uint4 src = *reinterpret_cast<const uint4*>(stg + item * 16);
-    uint8_t* row = op + (r >> 3) * 1024 + (r & 7) * 128;
-    const int x = r & 7;
-    const int c0 = i * CHUNKS;
+// packed bytes = 2 (BITS 4) or 4 (BITS 2) output chunks.  NT threads split the
+// items; thread t handles items t, t + NT, ... which all share the same chunk
+// index and row phase (r mod 8), so every address is a per-thread base plus a
+// compile-time offset.
+template <int BITS, int ROWS, int NT>
+__device__ __forceinline__ void unpack_stage(const uint8_t* __restrict__ stg, uint8_t* __restrict__ op, int tid) {
+  constexpr int IPR = BITS;                   // items per row: 16*BITS packed bytes / 16
+  constexpr int CHUNKS = 8 / IPR;             // output chunks per item
+  constexpr int ITEMS = ROWS * IPR;
+  static_assert(ITEMS % NT == 0, "items must split evenly");
+  constexpr int ROW_STEP = NT / IPR;          // rows advanced per pass
+  static_assert(ROW_STEP % 8 == 0, "row step must keep the swizzle phase");
+  const int r0 = tid / IPR, i = tid % IPR;
+  const int x = r0 & 7;
+  const uint8_t* src = stg + tid * 16;
+  uint8_t* row = op + (r0 >> 3) * 1024 + x * 128;
+  const int c0 = i * CHUNKS;
+#pragma unroll
+  for (int j = 0; j < ITEMS / NT; ++j) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src + j * NT * 16);
+    uint8_t* dst = row + j * (ROW_STEP / 8) * 1024;
     if constexpr (BITS == 4) {
-      const uint2 a = unpack_w4_word(src.x), b = unpack_w4_word(src.y);
-      const uint2 c = unpack_w4_word(src.z), d = unpack_w4_word(src.w);
-      *reinterpret_cast<uint4*>(row + (((c0 + 0) ^ x) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
-      *reinterpret_cast<uint4*>(row + (((c0 + 1) ^ x) << 4)) = make_uint4(c.x, c.y, d.x, d.y);
+      const uint2 a = unpack_w4_word(v.x), b = unpack_w4_word(v.y);
+      const uint2 c = unpack_w4_word(v.z), d = unpack_w4_word(v.w);
+      *reinterpret_cast<uint4*>(dst + (((c0 + 0) ^ x) << 4)) = make_uint4(a.x, a.y, b.x, b.y);
+      *reinterpret_cast<uint4*>(dst + (((c0 + 1) ^ x) << 4)) = make_uint4(c.x, c.y, d.x, d.y);
     } else {
       static_assert(BITS == 2, "BITS");
-      *reinterpret_cast<uint4*>(row + (((c0 + 0) ^ x) << 4)) = unpack_w2_word(src.x);
-      *reinterpret_cast<uint4*>(row + (((c0 + 1) ^ x) << 4)) = unpack_w2_word(src.y);
-      *reinterpret_cast<uint4*>(row + (((c0 + 2) ^ x) << 4)) = unpack_w2_word(src.z);
-      *reinterpret_cast<uint4*>(row + (((c0 + 3) ^ x) << 4)) = unpack_w2_word(src.w);
+      *reinterpret_cast<uint4*>(dst + (((c0 + 0) ^ x) << 4)) = unpack_w2_word(v.x);
+      *reinterpret_cast<uint4*>(dst + (((c0 + 1) ^ x) << 4)) = unpack_w2_word(v.y);
+      *reinterpret_cast<uint4*>(dst + (((c0 + 2) ^ x) << 4)) = unpack_w2_word(v.z);
+      *reinterpret_cast<uint4*>(dst + (((c0 + 3) ^ x) << 4)) = unpack_w2_word(v.w);
     }
   }
 }
@@ -154,7 +162,7 @@ __device__ __forceinline__ void accumulate(float2* acc, const uint32_t (&d)[H], 
 template <int H>
 __device__ __forceinline__ void store_dots(const GemmParams& p, int m, int col, int g, const uint32_t (&d)[H],
                                            int shift) {
-  if (m >= p.M) return;
+  if (m >= p.M || g >= p.G) return;
 #pragma unroll
   for (int j = 0; j < H; ++j) {
     const int n = col + j;
@@ -211,20 +219,31 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int issued = 0;
+    // Lane 0 loads the activation tile and lane 1 the weight tile of a stage
+    // with ONE bulk-tensor instruction: copies issued by successive
+    // instructions of a thread are serviced one after another (about one L2
+    // round trip each), while the lanes of one instruction proceed together.
+    int issued = 0;
+    if (lane < 2) {
+      const CUtensorMap* map = lane == 0 ? &tm_act : &tm_wgt;
+      const int x_step = lane == 0 ? C::KS * A / 8 : C::KS * W / 8;
+      const int y = lane == 0 ? m0 : n0;
+      const uint32_t dst_off = lane == 0 ? (A < 8 ? C::OP_A_BYTES + C::OP_W_BYTES : 0)
+                                         : (W < 8 ? C::OP_A_BYTES + C::OP_W_BYTES + C::STG_A_BYTES : C::OP_A_BYTES);
       for (int it = 0; it < n_iters; ++it) {
         const int s = it % C::STAGES;
-        if (!mbar_wait(&empty_bar[s], ((it / C::STAGES) & 1) ^ 1, kSiteProducer)) break;
-        uint8_t* st = smem + s * C::STAGE_BYTES;
-        uint8_t* dst_a = (A < 8) ? st + C::OP_A_BYTES + C::OP_W_BYTES : st;
-        uint8_t* dst_w = (W < 8) ? st + C::OP_A_BYTES + C::OP_W_BYTES + C::STG_A_BYTES : st + C::OP_A_BYTES;
-        mbar_arrive_expect_tx(&full_raw[s], C::TX_BYTES);
-        tma_load_2d(dst_a, &tm_act, it * (C::KS * A / 8), m0, &full_raw[s]);
-        tma_load_2d(dst_w, &tm_wgt, it * (C::KS * W / 8), n0, &full_raw[s]);
+        bool ok = true;
+        if (lane == 0) {
+          ok = mbar_wait(&empty_bar[s], ((it / C::STAGES) & 1) ^ 1, kSiteProducer);
+          if (ok) mbar_arrive_expect_tx(&full_raw[s], C::TX_BYTES);
+        }
+        if (!__shfl_sync(0x3u, ok, 0)) break;
+        tma_load_2d(smem + s * C::STAGE_BYTES + dst_off, map, it * x_step, y, &full_raw[s]);
         ++issued;
       }
-      // Never leave the CTA with bulk copies still landing in shared memory.
+    }
+    // Never leave the CTA with bulk copies still landing in shared memory.
+    if (lane == 0) {
       for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it)
         mbar_wait(&full_raw[it % C::STAGES], (it / C::STAGES) & 1, kSiteDrain);
     }
@@ -248,12 +267,12 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
         const uint64_t da = desc_a0 + kStageStep * s;
         const uint64_t dw = desc_w0 + kStageStep * s;
         const uint32_t d0 = tmem_base + pr * (2 * BN);
-        mma_i8(d0, da + 0, dw + 0, idesc, 0u);  // group 2it:   K bytes 0..31
-        mma_i8(d0, da + 2, dw + 2, idesc, 1u);  //              K bytes 32..63
-        if (2 * it + 1 < G) {
-          mma_i8(d0 + BN, da + 4, dw + 4, idesc, 0u);  // group 2it+1: K bytes 64..95
-          mma_i8(d0 + BN, da + 6, dw + 6, idesc, 1u);  //              K bytes 96..127
-        }
+        // Always both groups: past the end of K (odd G) the tiles are the
+        // TMA's zero fill, the dots are 0 and the epilogue gives them scale 0.
+        mma_i8(d0, da + 0, dw + 0, idesc, 0u);       // group 2it:   K bytes 0..31
+        mma_i8(d0, da + 2, dw + 2, idesc, 1u);       //              K bytes 32..63
+        mma_i8(d0 + BN, da + 4, dw + 4, idesc, 0u);  // group 2it+1: K bytes 64..95
+        mma_i8(d0 + BN, da + 6, dw + 6, idesc, 1u);  //              K bytes 96..127
         mma_commit(&acc_full[pr]);
         mma_commit(&empty_bar[s]);
       }
@@ -268,9 +287,9 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
         const int s = it % C::STAGES;
         if (!mbar_wait(&full_raw[s], (it / C::STAGES) & 1, kSiteConverter)) break;
         uint8_t* st = smem + s * C::STAGE_BYTES;
-        if constexpr (A < 8) unpack_stage<A, C::BM>(st + C::OP_A_BYTES + C::OP_W_BYTES, st, ctid, 64);
+        if constexpr (A < 8) unpack_stage<A, C::BM, 64>(st + C::OP_A_BYTES + C::OP_W_BYTES, st, ctid);
         if constexpr (W < 8)
-          unpack_stage<W, BN>(st + C::OP_A_BYTES + C::OP_W_BYTES + C::STG_A_BYTES, st + C::OP_A_BYTES, ctid, 64);
+          unpack_stage<W, BN, 64>(st + C::OP_A_BYTES + C::OP_W_BYTES + C::STG_A_BYTES, st + C::OP_A_BYTES, ctid);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full_op[s]);
@@ -326,22 +345,22 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
         const int pr = it % C::NPAIR;
         const uint32_t base = lane_base + pr * (2 * BN);
         const int g0 = 2 * it;
-        const bool second = g0 + 1 < G;
+        // Past the end of K (odd G) the second group's dots are 0 and s1 is 0
+        // (scale_at), so acc += 0 * 0 leaves every accumulator unchanged (an
+        // accumulator is never -0: it starts at +0 and the scales are > 0).
         const float s0 = s0raw * shift_scale, s1 = s1raw * shift_scale;
         tmem_ld<H>(base + H, rb);
         if constexpr (DOTS) store_dots<H>(p, m, col0, g0, ra, C::SHIFT);
         else accumulate<H>(acc, ra, s0);
         tmem_wait_ld();
-        if (second) {
-          tmem_ld<H>(base + BN, ra);
-          if constexpr (DOTS) store_dots<H>(p, m, col0 + H, g0, rb, C::SHIFT);
-          else accumulate<H>(acc + H / 2, rb, s0);
-          tmem_wait_ld();
-          tmem_ld<H>(base + BN + H, rb);
-          if constexpr (DOTS) store_dots<H>(p, m, col0, g0 + 1, ra, C::SHIFT);
-          else accumulate<H>(acc, ra, s1);
-          tmem_wait_ld();
-        }
+        tmem_ld<H>(base + BN, ra);
+        if constexpr (DOTS) store_dots<H>(p, m, col0 + H, g0, rb, C::SHIFT);
+        else accumulate<H>(acc + H / 2, rb, s0);
+        tmem_wait_ld();
+        tmem_ld<H>(base + BN + H, rb);
+        if constexpr (DOTS) store_dots<H>(p, m, col0, g0 + 1, ra, C::SHIFT);
+        else accumulate<H>(acc, ra, s1);
+        tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[pr]);
@@ -354,8 +373,8 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
             tmem_ld<H>(lane_base + pn * (2 * BN), ra);
           }
         }
-        if constexpr (DOTS) store_dots<H>(p, m, col0 + H, second ? g0 + 1 : g0, rb, C::SHIFT);
-        else accumulate<H>(acc + H / 2, rb, second ? s1 : s0);
+        if constexpr (DOTS) store_dots<H>(p, m, col0 + H, g0 + 1, rb, C::SHIFT);
+        else accumulate<H>(acc + H / 2, rb, s1);
         tmem_wait_ld();
       };
       // Scale slots: x for even stages, y for odd stages (fetched two stages ahead).
