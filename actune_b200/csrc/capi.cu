@@ -62,19 +62,44 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 bool valid_float_dtype(int t) { return t == ACTUNE_DTYPE_F32 || t == ACTUNE_DTYPE_F16 || t == ACTUNE_DTYPE_BF16; }
 size_t dtype_size(int t) { return t == ACTUNE_DTYPE_F32 ? 4 : 2; }
 
-// 2D uint8 tensor map [rows, row_bytes] with a box of [box_rows, box_bytes].
+// 2D uint8 tensor map [rows, row_bytes] with a box of [box_rows, box_bytes]; the
+// shared-memory swizzle span equals the box row width (32, 64 or 128 bytes) or none.
+enum class Swz { None, B32, B64, B128 };
+CUtensorMapSwizzle swizzle_mode(Swz z) {
+  switch (z) {
+    case Swz::B32: return CU_TENSOR_MAP_SWIZZLE_32B;
+    case Swz::B64: return CU_TENSOR_MAP_SWIZZLE_64B;
+    case Swz::B128: return CU_TENSOR_MAP_SWIZZLE_128B;
+    default: return CU_TENSOR_MAP_SWIZZLE_NONE;
+  }
+}
 int encode_map(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows,
-               bool swizzle128) {
+               Swz swz) {
   const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
   const cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        swizzle_mode(swz),
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? ACTUNE_OK : ACTUNE_ERR_CUDA;
 }
+
+// Token tile of the weights-in-TMEM kernel: the smallest of 16/32/64/128 that
+// holds M, else 128.
+int pick_wt(int variant, int64_t M) {
+  switch (variant) {
+    case ACTUNE_VARIANT_WT16: return 16;
+    case ACTUNE_VARIANT_WT32: return 32;
+    case ACTUNE_VARIANT_WT64: return 64;
+    case ACTUNE_VARIANT_WT128: return 128;
+    default: break;
+  }
+  return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+}
+
+bool is_wt_variant(int variant) { return variant >= ACTUNE_VARIANT_WT16; }
 
 int pick_bn(int variant, int64_t M, int64_t N, int num_sms) {
   switch (variant) {
@@ -110,6 +135,27 @@ cudaError_t dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, co
   }
 }
 
+template <int W, int A>
+cudaError_t dispatch_wt(int bt, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, cudaStream_t s) {
+  switch (bt) {
+    case 16: return launch_wt_gemm<W, A, 16>(ta, tw, p, s);
+    case 32: return launch_wt_gemm<W, A, 32>(ta, tw, p, s);
+    case 64: return launch_wt_gemm<W, A, 64>(ta, tw, p, s);
+    default: return launch_wt_gemm<W, A, 128>(ta, tw, p, s);
+  }
+}
+
+cudaError_t dispatch_wt_gemm(int W, int A, int bt, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
+                             cudaStream_t s) {
+#define ACTUNE_CASE(WW, AA) \
+  if (W == WW && A == AA) return dispatch_wt<WW, AA>(bt, ta, tw, p, s);
+  ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
+  ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
+  ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
+#undef ACTUNE_CASE
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t dispatch_gemm(int W, int A, int bn, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
                           cudaStream_t s) {
 #define ACTUNE_CASE(WW, AA) \
@@ -136,11 +182,20 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   if (rc != ACTUNE_OK) return rc;
   if (M == 0 || N == 0) return ACTUNE_OK;
   if (!aligned(a, 16) || !aligned(w, 16)) return ACTUNE_ERR_MISALIGNED;
-  const int bn = pick_bn(variant, M, N, g_devices[dev].num_sms);
+  const bool wt = is_wt_variant(variant);
+  const int bn = wt ? pick_wt(variant, M) : pick_bn(variant, M, N, g_devices[dev].num_sms);
   CUtensorMap ta, tw;
-  rc = encode_map(&ta, a, M, K * A / 8, A == 8 ? 128 : 16 * A, 128, A == 8);
+  // Token tile: int8 rows land in the SW128 operand layout; packed sub-byte rows are
+  // staged unswizzled for the in-kernel expansion.
+  rc = encode_map(&ta, a, M, K * A / 8, A == 8 ? 128 : 16 * A, wt ? bn : 128, A == 8 ? Swz::B128 : Swz::None);
   if (rc != ACTUNE_OK) return rc;
-  rc = encode_map(&tw, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn, W == 8);
+  if (wt) {
+    // Weight tile [128 rows x 16*W bytes] with the swizzle whose span is the row width,
+    // read row-per-thread by the converters without bank conflicts.
+    rc = encode_map(&tw, w, N, K * W / 8, 16 * W, 128, W == 8 ? Swz::B128 : (W == 4 ? Swz::B64 : Swz::B32));
+  } else {
+    rc = encode_map(&tw, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn, W == 8 ? Swz::B128 : Swz::None);
+  }
   if (rc != ACTUNE_OK) return rc;
   GemmParams p{};
   p.act_scale = a_scale;
@@ -155,7 +210,8 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
   p.out_dtype = out_dtype;
   p.out_vec_ok = (N % 8 == 0) && aligned(out, 16);
-  return dispatch_gemm(W, A, bn, ta, tw, p, stream) == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+  const cudaError_t e = wt ? dispatch_wt_gemm(W, A, bn, ta, tw, p, stream) : dispatch_gemm(W, A, bn, ta, tw, p, stream);
+  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
 }
 
 }  // namespace
@@ -199,7 +255,7 @@ int actune_packed_linear(const uint8_t* a, const float* a_scale, const uint8_t* 
                          int W, int A, int variant, void* stream) {
   int rc = check_gemm_shape(M, N, K, W, A);
   if (rc != ACTUNE_OK) return rc;
-  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_BN128) return ACTUNE_ERR_INVALID_VALUE;
+  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_WT128) return ACTUNE_ERR_INVALID_VALUE;
   if (bias != nullptr && !valid_float_dtype(bias_dtype)) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && N > 0 && (a == nullptr || a_scale == nullptr || w == nullptr || w_scale == nullptr || out == nullptr))
     return ACTUNE_ERR_INVALID_VALUE;
@@ -218,7 +274,7 @@ int actune_packed_linear_dots(const uint8_t* a, const uint8_t* w, int32_t* dots,
                               int W, int A, int variant, void* stream) {
   int rc = check_gemm_shape(M, N, K, W, A);
   if (rc != ACTUNE_OK) return rc;
-  if (variant < 0 || variant > ACTUNE_VARIANT_BN128) return ACTUNE_ERR_INVALID_VALUE;
+  if (variant < 0 || variant > ACTUNE_VARIANT_WT128) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && N > 0 && (a == nullptr || w == nullptr || dots == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
   if (!aligned(dots, 4)) return ACTUNE_ERR_MISALIGNED;
   return run_gemm(a, nullptr, w, nullptr, nullptr, kDtNone, nullptr, kDtF32, dots, M, N, K, W, A, variant,

@@ -66,7 +66,9 @@ struct Group64Cfg {
   static constexpr int STAGE_RAW = OP_A_BYTES + OP_W_BYTES + STG_A_BYTES + STG_W_BYTES;
   static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
   static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  // A multiple of NPAIR, so that the accumulator pair of an unrolled ring slot is a
+  // compile-time constant.
+  static constexpr int STAGES = (STAGES_FIT > 8 ? 8 : STAGES_FIT) / NPAIR * NPAIR;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
   // Bytes one stage's two TMA loads deliver (full boxes; OOB parts are zero-filled).
   static constexpr uint32_t TX_BYTES = BM * KS * A / 8 + BN * KS * W / 8;
@@ -223,6 +225,9 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
     // with ONE bulk-tensor instruction: copies issued by successive
     // instructions of a thread are serviced one after another (about one L2
     // round trip each), while the lanes of one instruction proceed together.
+    // The loop is unrolled over the ring and every operand of a copy sits in a
+    // register of its own: an asynchronous copy reads its register operands some
+    // time after issue, and rewriting one for the next copy stalls until it has.
     int issued = 0;
     if (lane < 2) {
       const CUtensorMap* map = lane == 0 ? &tm_act : &tm_wgt;
@@ -230,16 +235,33 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
       const int y = lane == 0 ? m0 : n0;
       const uint32_t dst_off = lane == 0 ? (A < 8 ? C::OP_A_BYTES + C::OP_W_BYTES : 0)
                                          : (W < 8 ? C::OP_A_BYTES + C::OP_W_BYTES + C::STG_A_BYTES : C::OP_A_BYTES);
-      for (int it = 0; it < n_iters; ++it) {
-        const int s = it % C::STAGES;
-        bool ok = true;
-        if (lane == 0) {
-          ok = mbar_wait(&empty_bar[s], ((it / C::STAGES) & 1) ^ 1, kSiteProducer);
-          if (ok) mbar_arrive_expect_tx(&full_raw[s], C::TX_BYTES);
+      constexpr int S = C::STAGES, HALF = C::STAGES / 2;
+      uint32_t dst[S], bar[S];
+      int xs[S];
+#pragma unroll
+      for (int j = 0; j < S; ++j) {
+        dst[j] = smem_u32(smem + j * C::STAGE_BYTES + dst_off);
+        bar[j] = smem_u32(&full_raw[j]);
+        xs[j] = j * x_step;
+      }
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int it0 = 0; it0 < n_iters && ok; it0 += S) {
+#pragma unroll
+        for (int j = 0; j < S; ++j) {
+          if (it0 + j >= n_iters) break;
+          bool w_ok = true;
+          if (lane == 0) {
+            w_ok = mbar_wait(&empty_bar[j], ph ^ 1, kSiteProducer);
+            if (w_ok) mbar_arrive_expect_tx(&full_raw[j], C::TX_BYTES);
+          }
+          if (!__shfl_sync(0x3u, w_ok, 0)) { ok = false; break; }
+          if (j + HALF < S) xs[j + HALF] = (it0 + j + HALF) * x_step;  // read HALF copies from now
+          tma_load_2d_u32(dst[j], map, xs[j], y, bar[j]);
+          ++issued;
+          if (j >= HALF) xs[j - HALF] = (it0 + S + j - HALF) * x_step;  // its copy went HALF ago
         }
-        if (!__shfl_sync(0x3u, ok, 0)) break;
-        tma_load_2d(smem + s * C::STAGE_BYTES + dst_off, map, it * x_step, y, &full_raw[s]);
-        ++issued;
+        ph ^= 1;
       }
     }
     // Never leave the CTA with bulk copies still landing in shared memory.
@@ -249,32 +271,67 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Straight-line per stage: wait operands, wait the accumulator pair,
-    // 4 MMAs, 2 commits.  Descriptors differ only in their start-address field
-    // (16-byte units): +2 per 32-byte K step, +STAGE_BYTES/16 per stage.
+    // Per stage: wait operands, wait the accumulator pair, 4 MMAs, 2 commits.
+    // An MMA reads its register operands when the tensor core takes it, so the
+    // descriptors live in two register sets used by alternate stages and each set
+    // is rewritten only after the other stage's MMAs have been issued.
     if (lane == 0) {
+      constexpr int S = C::STAGES;
       constexpr uint32_t idesc = idesc_i8(C::BM, BN);
       const uint64_t desc_a0 = smem_desc_sw128(smem_u32(smem));
       const uint64_t desc_w0 = smem_desc_sw128(smem_u32(smem) + C::OP_A_BYTES);
       constexpr uint64_t kStageStep = (uint64_t)(C::STAGE_BYTES >> 4);
-      for (int it = 0; it < n_iters; ++it) {
-        const int s = it % C::STAGES;
-        const int pr = it % C::NPAIR;
-        uint64_t* ready = C::CONVERT ? &full_op[s] : &full_raw[s];
-        if (!mbar_wait(ready, (it / C::STAGES) & 1, kSiteMmaFull)) break;
-        if (!mbar_wait(&acc_empty[pr], ((it / C::NPAIR) & 1) ^ 1, kSiteMmaAcc)) break;
-        tc_fence_after();
-        const uint64_t da = desc_a0 + kStageStep * s;
-        const uint64_t dw = desc_w0 + kStageStep * s;
-        const uint32_t d0 = tmem_base + pr * (2 * BN);
-        // Always both groups: past the end of K (odd G) the tiles are the
-        // TMA's zero fill, the dots are 0 and the epilogue gives them scale 0.
-        mma_i8(d0, da + 0, dw + 0, idesc, 0u);       // group 2it:   K bytes 0..31
-        mma_i8(d0, da + 2, dw + 2, idesc, 1u);       //              K bytes 32..63
-        mma_i8(d0 + BN, da + 4, dw + 4, idesc, 0u);  // group 2it+1: K bytes 64..95
-        mma_i8(d0 + BN, da + 6, dw + 6, idesc, 1u);  //              K bytes 96..127
-        mma_commit(&acc_full[pr]);
-        mma_commit(&empty_bar[s]);
+      uint64_t da[2][4], dw[2][4];
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          da[q][k] = desc_a0 + kStageStep * q + 2 * k;
+          dw[q][k] = desc_w0 + kStageStep * q + 2 * k;
+        }
+      uint32_t dacc[C::NPAIR][2], bacc[C::NPAIR], bempty[S];
+#pragma unroll
+      for (int pr = 0; pr < C::NPAIR; ++pr) {
+        dacc[pr][0] = tmem_base + pr * (2 * BN);
+        dacc[pr][1] = tmem_base + pr * (2 * BN) + BN;
+        bacc[pr] = smem_u32(&acc_full[pr]);
+      }
+#pragma unroll
+      for (int j = 0; j < S; ++j) bempty[j] = smem_u32(&empty_bar[j]);
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int it0 = 0; it0 < n_iters && ok; it0 += S) {
+#pragma unroll
+        for (int j = 0; j < S; ++j) {
+          const int it = it0 + j;
+          if (it >= n_iters) break;
+          const int pr = j % C::NPAIR;
+          const int q = j & 1;
+          uint64_t* ready = C::CONVERT ? &full_op[j] : &full_raw[j];
+          if (!mbar_wait(ready, ph, kSiteMmaFull) ||
+              !mbar_wait(&acc_empty[pr], ((it / C::NPAIR) & 1) ^ 1, kSiteMmaAcc)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // Always both groups: past the end of K (odd G) the tiles are the
+          // TMA's zero fill, the dots are 0 and the epilogue gives them scale 0.
+          mma_i8(dacc[pr][0], da[q][0], dw[q][0], idesc, 0u);  // group 2it:   K bytes 0..31
+          mma_i8(dacc[pr][0], da[q][1], dw[q][1], idesc, 1u);  //              K bytes 32..63
+          mma_i8(dacc[pr][1], da[q][2], dw[q][2], idesc, 0u);  // group 2it+1: K bytes 64..95
+          mma_i8(dacc[pr][1], da[q][3], dw[q][3], idesc, 1u);  //              K bytes 96..127
+          mma_commit_u32(bacc[pr]);
+          mma_commit_u32(bempty[j]);
+          // The other register set was read by the previous stage's MMAs, issued a
+          // whole stage ago; it now takes the next ring slot's descriptors.
+          const int jn = (j + 1) % S;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            da[q ^ 1][k] = desc_a0 + kStageStep * jn + 2 * k;
+            dw[q ^ 1][k] = desc_w0 + kStageStep * jn + 2 * k;
+          }
+        }
+        ph ^= 1;
       }
       mma_commit(&mma_done);
       mbar_wait(&mma_done, 0, kSiteMmaDone);

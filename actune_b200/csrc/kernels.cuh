@@ -2,6 +2,7 @@
 #pragma once
 
 #include "gemm_group64.cuh"
+#include "gemm_wt.cuh"
 
 namespace actune {
 

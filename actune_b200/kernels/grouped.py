@@ -106,7 +106,7 @@ class _Extension:
             raise RuntimeError("rank mismatch")
         m, k = source.shape
         variant = _lib.VARIANT_AUTO if config is None else int(config)
-        if variant < 0 or variant > _lib.VARIANT_BN128:
+        if variant < 0 or variant > _lib.VARIANT_MAX:
             raise RuntimeError("invalid configuration")
         with torch.cuda.device(source.device):
             return ops.packed_linear(a, as_, w, ws, None if bias.numel() == 0 else bias, k, int(W), int(A),

@@ -51,14 +51,21 @@ typedef enum actune_dtype {
   ACTUNE_DTYPE_BF16 = 3
 } actune_dtype;
 
-/* GEMM tile choice (the reference's `config` argument of grouped_big_m.cu:92-93
- * selects among its tile geometries the same way).  All variants compute the
- * identical fp32 chain, so their outputs are bit-identical. */
+/* GEMM kernel and tile choice (the reference's `config` argument of
+ * grouped_big_m.cu:92-93 selects among its tile geometries the same way).  All
+ * variants compute the identical fp32 chain, so their outputs are bit-identical.
+ * BN*: token rows on the MMA M side (128 per tile), BN weight rows per tile, both
+ * operands staged in shared memory.  WT*: weights-in-tensor-memory form, 128
+ * weight rows per tile expanded straight into TMEM, WT tokens per tile. */
 typedef enum actune_variant {
   ACTUNE_VARIANT_AUTO = 0,
   ACTUNE_VARIANT_BN32 = 1,
   ACTUNE_VARIANT_BN64 = 2,
-  ACTUNE_VARIANT_BN128 = 3
+  ACTUNE_VARIANT_BN128 = 3,
+  ACTUNE_VARIANT_WT16 = 4,
+  ACTUNE_VARIANT_WT32 = 5,
+  ACTUNE_VARIANT_WT64 = 6,
+  ACTUNE_VARIANT_WT128 = 7
 } actune_variant;
 
 /* Device error codes reported by actune_device_error(). */

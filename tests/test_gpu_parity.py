@@ -139,7 +139,7 @@ def test_gemm_golden(ops, gemm_golden, w, a, si):
     pw = torch.from_numpy(g[f"{key}_pw"]).to(DEV)
     ws = torch.from_numpy(g[f"{key}_ws"]).to(DEV)
     bias = f32_of_bits(g[f"s{si}_bias"]).to(DEV)
-    for variant in (0, 1, 2, 3):
+    for variant in range(8):  # AUTO, BN32/64/128 and the weights-in-TMEM WT16/32/64/128
         dots = ops.packed_linear_dots(pa, pw, k, w, a, variant=variant).cpu().numpy()
         ref = g[f"{key}_dots"]
         assert np.array_equal(dots[: ref.shape[0]], ref), f"dots variant {variant}"
@@ -183,6 +183,16 @@ def test_gemm_random_bit_exact(ops, w, a, m, k, n):
     assert_bits(bf16_bits(y), O.to_bf16_bits(ref), "bf16 output")
 
 
+@pytest.mark.parametrize("w,a", PAIRS)
+@pytest.mark.parametrize("variant", [4, 5, 6, 7])
+def test_gemm_weights_in_tmem_variants(ops, w, a, variant):
+    """The weights-in-TMEM kernel (explicit WT variants) on ragged shapes: partial
+    weight tiles, partial token tiles and an odd number of K groups."""
+    for m, k, n in [(37, 448, 200), (130, 1024, 136)]:
+        y, ref, _ = _case(ops, m, k, n, w, a, seed=m + k + n + variant, variant=variant)
+        assert_bits(bf16_bits(y), O.to_bf16_bits(ref), f"bf16 output m={m} k={k} n={n}")
+
+
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("bias_dtype", [None, torch.float32, torch.float16, torch.bfloat16])
 def test_gemm_dtypes(ops, out_dtype, bias_dtype):
@@ -215,6 +225,7 @@ def test_gemm_dots_full_size_properties(ops):
     d0 = ops.packed_linear_dots(pa, pw, k, w, a, variant=3)
     d1 = ops.packed_linear_dots(pa, pw, k, w, a, variant=1)
     assert torch.equal(d0, d1)
+    assert torch.equal(d0, ops.packed_linear_dots(pa, pw, k, w, a, variant=7))
     rows = [0, 99, 511, 599]
     ref = O.group_dots(pa.cpu().numpy()[rows], pw.cpu().numpy(), k, w, a)
     assert np.array_equal(d0.cpu().numpy()[rows], ref)
