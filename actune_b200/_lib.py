@@ -26,7 +26,8 @@ ERR_WORKSPACE = 5
 DTYPE_NONE, DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2, 3
 VARIANT_AUTO, VARIANT_BN32, VARIANT_BN64, VARIANT_BN128 = 0, 1, 2, 3
 VARIANT_WT16, VARIANT_WT32, VARIANT_WT64, VARIANT_WT128 = 4, 5, 6, 7
-VARIANT_MAX = VARIANT_WT128
+VARIANT_GEMV = 8
+VARIANT_MAX = VARIANT_GEMV
 
 # Every symbol the header declares (checked by the CPU test suite).
 EXPORTS = (
@@ -41,6 +42,7 @@ EXPORTS = (
     "actune_status_string",
     "actune_device_error",
     "actune_abi_version",
+    "actune_last_cuda_error",
 )
 
 _LIB = None
@@ -70,6 +72,7 @@ def _declare(L):
     L.actune_status_string.restype = ctypes.c_char_p
     L.actune_device_error.argtypes = [ctypes.POINTER(i32), ctypes.POINTER(i32), i32]
     L.actune_abi_version.argtypes = []
+    L.actune_last_cuda_error.argtypes = []
     for name in EXPORTS:
         if name not in ("actune_status_string", "actune_grouped_linear_workspace_size"):
             getattr(L, name).restype = i32
@@ -97,6 +100,8 @@ def status_string(status: int) -> str:
 def check(status: int, what: str = "") -> None:
     if status != OK:
         msg = f"actune_b200{(' ' + what) if what else ''}: {status_string(status)} (status {status})"
+        if status == ERR_CUDA:
+            msg += f" [cudaError {lib().actune_last_cuda_error()}]"
         raise ActuneError(status, msg)
 
 

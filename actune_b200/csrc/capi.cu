@@ -57,6 +57,14 @@ int current_device(int* dev_out) {
   return ACTUNE_OK;
 }
 
+// CUDA error behind the last ACTUNE_ERR_CUDA returned on this thread.
+thread_local int g_last_cuda_error = 0;
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return ACTUNE_OK;
+  g_last_cuda_error = (int)e;
+  return ACTUNE_ERR_CUDA;
+}
+
 bool valid_bits(int b) { return b == 2 || b == 4 || b == 8; }
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 bool valid_float_dtype(int t) { return t == ACTUNE_DTYPE_F32 || t == ACTUNE_DTYPE_F16 || t == ACTUNE_DTYPE_BF16; }
@@ -99,7 +107,11 @@ int pick_wt(int variant, int64_t M) {
   return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
 }
 
-bool is_wt_variant(int variant) { return variant >= ACTUNE_VARIANT_WT16; }
+bool is_wt_variant(int variant) { return variant >= ACTUNE_VARIANT_WT16 && variant <= ACTUNE_VARIANT_WT128; }
+
+bool use_gemv(int variant, int64_t M) {
+  return variant == ACTUNE_VARIANT_GEMV || (variant == ACTUNE_VARIANT_AUTO && M <= 32);
+}
 
 int pick_bn(int variant, int64_t M, int64_t N, int num_sms) {
   switch (variant) {
@@ -182,6 +194,29 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   if (rc != ACTUNE_OK) return rc;
   if (M == 0 || N == 0) return ACTUNE_OK;
   if (!aligned(a, 16) || !aligned(w, 16)) return ACTUNE_ERR_MISALIGNED;
+  if (use_gemv(variant, M)) {
+    if (M > 32) return ACTUNE_ERR_INVALID_VALUE;
+    CUtensorMap ta, tw;
+    const int tok = M <= 16 ? 16 : 32;
+    rc = encode_map(&ta, a, M, K * A / 8, 128, tok, Swz::B128);
+    if (rc != ACTUNE_OK) return rc;
+    rc = encode_map(&tw, w, N, K * W / 8, 128, kGemvRows, Swz::B128);
+    if (rc != ACTUNE_OK) return rc;
+    GemmParams p{};
+    p.act_scale = a_scale;
+    p.w_scale = w_scale;
+    p.bias = bias;
+    p.out = out;
+    p.dots = dots;
+    p.M = (int)M;
+    p.N = (int)N;
+    p.K = (int)K;
+    p.G = (int)(K / 64);
+    p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
+    p.out_dtype = out_dtype;
+    p.out_vec_ok = 0;
+    return cuda_status(launch_gemv_group64(W, A, ta, tw, p, stream));
+  }
   const bool wt = is_wt_variant(variant);
   const int bn = wt ? pick_wt(variant, M) : pick_bn(variant, M, N, g_devices[dev].num_sms);
   CUtensorMap ta, tw;
@@ -211,7 +246,7 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   p.out_dtype = out_dtype;
   p.out_vec_ok = (N % 8 == 0) && aligned(out, 16);
   const cudaError_t e = wt ? dispatch_wt_gemm(W, A, bn, ta, tw, p, stream) : dispatch_gemm(W, A, bn, ta, tw, p, stream);
-  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+  return cuda_status(e);
 }
 
 }  // namespace
@@ -222,6 +257,8 @@ using namespace actune;
 extern "C" {
 
 int actune_abi_version(void) { return ACTUNE_ABI_VERSION; }
+
+int actune_last_cuda_error(void) { return g_last_cuda_error; }
 
 const char* actune_status_string(int status) {
   switch (status) {
@@ -247,7 +284,7 @@ int actune_quantize_group64(const void* x, int x_dtype, int64_t M, int64_t K, in
   const int dt = x_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (x_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
   cudaError_t e = launch_quantize_group64(x, dt, M * (K / 64), A, packed, scales, g_devices[dev].num_sms,
                                           reinterpret_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+  return cuda_status(e);
 }
 
 int actune_packed_linear(const uint8_t* a, const float* a_scale, const uint8_t* w, const float* w_scale,
@@ -255,7 +292,7 @@ int actune_packed_linear(const uint8_t* a, const float* a_scale, const uint8_t* 
                          int W, int A, int variant, void* stream) {
   int rc = check_gemm_shape(M, N, K, W, A);
   if (rc != ACTUNE_OK) return rc;
-  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_WT128) return ACTUNE_ERR_INVALID_VALUE;
+  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_GEMV) return ACTUNE_ERR_INVALID_VALUE;
   if (bias != nullptr && !valid_float_dtype(bias_dtype)) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && N > 0 && (a == nullptr || a_scale == nullptr || w == nullptr || w_scale == nullptr || out == nullptr))
     return ACTUNE_ERR_INVALID_VALUE;
@@ -274,7 +311,7 @@ int actune_packed_linear_dots(const uint8_t* a, const uint8_t* w, int32_t* dots,
                               int W, int A, int variant, void* stream) {
   int rc = check_gemm_shape(M, N, K, W, A);
   if (rc != ACTUNE_OK) return rc;
-  if (variant < 0 || variant > ACTUNE_VARIANT_WT128) return ACTUNE_ERR_INVALID_VALUE;
+  if (variant < 0 || variant > ACTUNE_VARIANT_GEMV) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && N > 0 && (a == nullptr || w == nullptr || dots == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
   if (!aligned(dots, 4)) return ACTUNE_ERR_MISALIGNED;
   return run_gemm(a, nullptr, w, nullptr, nullptr, kDtNone, nullptr, kDtF32, dots, M, N, K, W, A, variant,
@@ -293,7 +330,7 @@ int actune_weight_codes(const void* weight, int dtype, int64_t N, int64_t K, int
     return ACTUNE_ERR_MISALIGNED;
   const int dt = dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
   cudaError_t e = launch_weight_codes(weight, dt, N, K, W, A, clip, codes, scale, reinterpret_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+  return cuda_status(e);
 }
 
 int actune_r4_refine(const void* weight, int dtype, int64_t N, int64_t K, const int8_t* q4, const float* scale4,
@@ -307,7 +344,7 @@ int actune_r4_refine(const void* weight, int dtype, int64_t N, int64_t K, const 
   if (!aligned(weight, dtype_size(dtype)) || !aligned(scale4, 4)) return ACTUNE_ERR_MISALIGNED;
   const int dt = dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
   cudaError_t e = launch_r4_refine(weight, dt, N, K, q4, scale4, residual, q8, reinterpret_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+  return cuda_status(e);
 }
 
 int actune_pack_rows(const int8_t* codes, int64_t R, int64_t K, int bits, uint8_t* packed, void* stream) {
@@ -318,7 +355,7 @@ int actune_pack_rows(const int8_t* codes, int64_t R, int64_t K, int bits, uint8_
   if (rc != ACTUNE_OK) return rc;
   cudaError_t e = launch_pack_rows(codes, R * (K * bits / 8), bits, packed, g_devices[dev].num_sms,
                                    reinterpret_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+  return cuda_status(e);
 }
 
 size_t actune_grouped_linear_workspace_size(int64_t M, int64_t K, int A) {

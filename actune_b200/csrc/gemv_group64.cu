@@ -1,0 +1,301 @@
+// Weight-streaming group-64 linear for few tokens (M <= 32): the decode / denoise
+// shape, where the work is bound by reading the packed weights from HBM.
+//
+//   y[m, n] = ws[n] * sum_g ( float(dot_g(m, n)) * as[m, g] )  (+ bias[n])
+//
+// with the same exact int32 group dots and the same fp32 chain as the tile kernels
+// (actune/kernels/grouped.py:80-94, actune/kernels/grouped_native.cu:70-85):
+// acc = fma(float(dot_g), as[m, g], acc) for g = 0, 1, ... then fma(acc, ws, bias).
+//
+// A 128-row tensor-core tile would waste most of its work on 16 tokens and the
+// single-thread tcgen05 issue would bound it, so this kernel uses the warp-level
+// integer MMA (m16n8k32, s8 x s8 -> s32): each warp owns 8 weight rows and all
+// (up to 32) tokens and walks K group by group; a CTA of 4 warps covers 32 rows, so
+// N / 32 CTAs stream disjoint weight rows with no reduction across CTAs.
+//
+// Operands reach shared memory by TMA in 1024-wide K stages through a 3-4 deep ring
+// (96-192 KB in flight per CTA, enough to cover HBM latency), as 128-byte-wide boxes
+// with the 128-byte swizzle: a stage is [128 B block][row][128 B], 16-byte chunk c of
+// row r stored at chunk c ^ (r mod 8), so the lanes of a warp -- 8 rows x 4 lanes,
+// each reading its 16 consecutive codes of a 64-wide group -- spread over all banks.
+// K is permuted the same way for both operands inside each group (lane t takes codes
+// 16t..16t+15), which leaves every dot unchanged.  Sub-byte codes go to the top bits
+// of int8 (code * 2^(8-bits)); the power of two is removed exactly from the
+// activation scale.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace actune {
+
+template <int W, int A, int MT>
+struct GemvCfg {
+  static constexpr int ROWS = 32;                 // weight rows per CTA (4 warps x 8)
+  static constexpr int TOK = 16 * MT;             // token rows staged per CTA
+  static constexpr int KSTG = 1024;               // K per stage (16 groups)
+  static constexpr int GPS = KSTG / 64;           // groups per stage
+  static constexpr int A_BLK = KSTG * A / 8 / 128;  // 128-byte blocks per token row per stage (= boxes)
+  static constexpr int W_BLK = KSTG * W / 8 / 128;  // 128-byte blocks per weight row per stage
+  static constexpr int A_BYTES = A_BLK * TOK * 128;
+  static constexpr int W_BYTES = W_BLK * ROWS * 128;
+  static_assert(A_BLK + W_BLK <= 32, "one box per producer lane");
+  static constexpr int STAGE_BYTES = (A_BYTES + W_BYTES + 1023) / 1024 * 1024;
+  static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;  // 3 for W8A8 with 32 tokens, else 4
+  static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
+  static_assert(STAGES >= 2, "ring depth");
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  static constexpr int SHIFT = (8 - A) + (8 - W);
+  static constexpr int THREADS = 128;
+};
+
+__device__ __forceinline__ void mma_s8_16832(int32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Sixteen codes (lane t's part of 64-wide group g) of row r of a staged operand as
+// four int8x4 words in K order.  `rows` is the row count of one box; the stage holds
+// [block][row][128 B] with the 128-byte swizzle.
+template <int BITS>
+__device__ __forceinline__ uint4 load_codes16(const uint8_t* tile, int rows, int r, int g, int t) {
+  const int off = g * 8 * BITS + t * 2 * BITS;  // byte offset of the lane's codes within the stage row
+  const int blk = off >> 7, c = (off >> 4) & 7, sub = off & 15;
+  const uint8_t* addr = tile + (blk * rows + r) * 128 + ((c ^ (r & 7)) << 4) + sub;
+  if constexpr (BITS == 8) {
+    return *reinterpret_cast<const uint4*>(addr);
+  } else if constexpr (BITS == 4) {
+    const uint2 v = *reinterpret_cast<const uint2*>(addr);
+    const uint2 lo = unpack_w4_word(v.x), hi = unpack_w4_word(v.y);
+    return make_uint4(lo.x, lo.y, hi.x, hi.y);
+  } else {
+    return unpack_w2_word(*reinterpret_cast<const uint32_t*>(addr));
+  }
+}
+
+enum : int { kGvSiteProducer = 31, kGvSiteFull, kGvSiteDrain };
+
+template <int W, int A, int MT, bool DOTS>
+__global__ void __launch_bounds__(128) gemv_group64_kernel(const __grid_constant__ CUtensorMap tm_act,
+                                                            const __grid_constant__ CUtensorMap tm_wgt,
+                                                            const GemmParams p) {
+  using C = GemvCfg<W, A, MT>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  // Activation scales of a stage, [group][token], times 2^-SHIFT; double-buffered
+  // and filled one stage ahead so no group waits on a global load.
+  __shared__ float sc_smem[2][C::GPS][C::TOK];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, t = lane & 3;
+  const int G = p.G;
+  const int n_stages = (G + C::GPS - 1) / C::GPS;
+  const int n0 = blockIdx.x * C::ROWS;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 4);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  // Producer: lanes 0 .. A_BLK-1 of warp 0 load the token boxes of a stage and the
+  // next W_BLK lanes its weight boxes, all in one instruction, S stages ahead.
+  constexpr int NBOX = C::A_BLK + C::W_BLK;
+  constexpr uint32_t PMASK = (NBOX >= 32) ? 0xffffffffu : ((1u << NBOX) - 1u);
+  auto issue = [&](int st) {
+    const int s = st % C::STAGES;
+    if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], C::A_BYTES + C::W_BYTES);
+    __syncwarp(PMASK);
+    uint8_t* base = smem + s * C::STAGE_BYTES;
+    if (lane < C::A_BLK)
+      tma_load_2d(base + lane * C::TOK * 128, &tm_act, (st * C::A_BLK + lane) * 128, 0, &full_bar[s]);
+    else
+      tma_load_2d(base + C::A_BYTES + (lane - C::A_BLK) * C::ROWS * 128, &tm_wgt,
+                  (st * C::W_BLK + lane - C::A_BLK) * 128, n0, &full_bar[s]);
+  };
+  int issued = 0;
+  if (warp == 0 && lane < NBOX) {
+    if (lane < 2) prefetch_tensormap(lane == 0 ? &tm_act : &tm_wgt);
+    for (int st = 0; st < n_stages && st < C::STAGES; ++st) {
+      issue(st);
+      ++issued;
+    }
+  }
+
+  const int row = warp * 8 + gid;  // weight row (within the CTA) this lane's B operand comes from
+  const float shift_scale = 1.0f / float(1 << C::SHIFT);
+  // Accumulators: tile mt, {token gid, rows 2t, 2t+1}, {token gid + 8, rows 2t, 2t+1}.
+  float acc[MT][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[mt][i] = 0.f;
+  // Cooperative scale staging: thread i covers entries i, i + 128, ... of the
+  // [GPS][TOK] block of a stage.
+  constexpr int SC_PER_THREAD = (C::GPS * C::TOK + 127) / 128;
+  auto load_scales = [&](int st, float (&v)[SC_PER_THREAD]) {
+#pragma unroll
+    for (int j = 0; j < SC_PER_THREAD; ++j) {
+      const int e = threadIdx.x + 128 * j;
+      const int gl = e / C::TOK, m = e % C::TOK;
+      const int g = st * C::GPS + gl;
+      v[j] = (!DOTS && e < C::GPS * C::TOK && m < p.M && g < G) ? __ldg(p.act_scale + (int64_t)m * G + g) * shift_scale
+                                                                 : 0.f;
+    }
+  };
+  auto store_scales = [&](int buf, const float (&v)[SC_PER_THREAD]) {
+#pragma unroll
+    for (int j = 0; j < SC_PER_THREAD; ++j) {
+      const int e = threadIdx.x + 128 * j;
+      if (e < C::GPS * C::TOK) (&sc_smem[buf][0][0])[e] = v[j];
+    }
+  };
+  float sc_next[SC_PER_THREAD];
+  load_scales(0, sc_next);
+  store_scales(0, sc_next);
+  if (n_stages > 1) load_scales(1, sc_next);
+  __syncthreads();
+
+  bool ok = true;
+  for (int st = 0; st < n_stages; ++st) {
+    const int s = st % C::STAGES;
+    // A failed wait only marks the CTA for exit; every thread still reaches the
+    // end-of-stage barrier below, so the exit is CTA-uniform and no barrier waits
+    // for a warp that has left.
+    if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[s], (st / C::STAGES) & 1, kGvSiteFull))) ok = false;
+    const uint8_t* a_tile = smem + s * C::STAGE_BYTES;
+    const uint8_t* w_tile = a_tile + C::A_BYTES;
+    // All 16 groups of a stage, unrolled: the shared-memory offsets become
+    // constants and independent groups overlap.  Groups past the end of K are the
+    // TMA's zero fill with scale 0 (acc += 0 * 0 leaves every accumulator as it is;
+    // an accumulator is never -0), so only the dots export has to skip them.
+#pragma unroll
+    for (int gl = 0; gl < C::GPS; ++gl) {
+      const int g = st * C::GPS + gl;
+      if (!ok) break;
+      float sc[MT][2];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) sc[mt][h] = sc_smem[st & 1][gl][mt * 16 + h * 8 + gid];
+      const uint4 wq = load_codes16<W>(w_tile, C::ROWS, row, gl, t);
+      int32_t d[MT][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const uint4 a_lo = load_codes16<A>(a_tile, C::TOK, mt * 16 + gid, gl, t);
+        const uint4 a_hi = load_codes16<A>(a_tile, C::TOK, mt * 16 + gid + 8, gl, t);
+        d[mt][0] = d[mt][1] = d[mt][2] = d[mt][3] = 0;
+        // K permutation inside the group: MMA chunk 0 takes codes 16t+0..7, chunk 1
+        // codes 16t+8..15 of this lane (both operands identically).
+        const uint32_t a0[4] = {a_lo.x, a_hi.x, a_lo.y, a_hi.y};
+        mma_s8_16832(d[mt], a0, wq.x, wq.y);
+        const uint32_t a1[4] = {a_lo.z, a_hi.z, a_lo.w, a_hi.w};
+        mma_s8_16832(d[mt], a1, wq.z, wq.w);
+      }
+      if constexpr (DOTS) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int m = mt * 16 + (i >> 1) * 8 + gid;
+            const int n = n0 + warp * 8 + 2 * t + (i & 1);
+            if (m < p.M && n < p.N && g < G) p.dots[((int64_t)m * p.N + n) * G + g] = d[mt][i] >> C::SHIFT;
+          }
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            acc[mt][i] = fmaf(__int2float_rn(d[mt][i]), sc[mt][i >> 1], acc[mt][i]);
+      }
+    }
+    // Publish the next stage's scales (its buffer was last read in stage st - 1,
+    // before the previous barrier) and fetch the ones after it.
+    if (st + 1 < n_stages) store_scales((st + 1) & 1, sc_next);
+    if (st + 2 < n_stages) load_scales(st + 2, sc_next);
+    // Release the stage; warp 0's producer lanes refill it once all 4 warps are done.
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);
+    if (ok && warp == 0 && lane < NBOX && st + C::STAGES < n_stages) {
+      bool w_ok = true;
+      if (lane == 0) w_ok = mbar_wait(&empty_bar[s], (st / C::STAGES) & 1, kGvSiteProducer);
+      if (__shfl_sync(PMASK, w_ok, 0)) {
+        issue(st + C::STAGES);
+        ++issued;
+      } else {
+        ok = false;
+      }
+    }
+    if (__syncthreads_or(!ok)) {
+      ok = false;
+      break;
+    }
+  }
+  // Never leave the CTA with bulk copies still landing in shared memory.
+  // (Only the last STAGES issued copies can still be pending; an older barrier
+  // phase cannot be waited for any more once its slot has been reused.)
+  if (warp == 0 && lane == 0) {
+    for (int st = issued > C::STAGES ? issued - C::STAGES : 0; st < issued; ++st)
+      mbar_wait(&full_bar[st % C::STAGES], (st / C::STAGES) & 1, kGvSiteDrain);
+  }
+
+  if constexpr (!DOTS) {
+    if (ok) {
+#pragma unroll
+      for (int i2 = 0; i2 < 2; ++i2) {
+        const int n = n0 + warp * 8 + 2 * t + i2;
+        if (n >= p.N) continue;
+        const float ws = __ldg(p.w_scale + n);
+        const bool has_bias = p.bias_dtype != kDtNone;
+        const float bias = has_bias ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int m = mt * 16 + h * 8 + gid;
+            if (m >= p.M) continue;
+            const float a = acc[mt][h * 2 + i2];
+            store_scalar(p, (int64_t)m * p.N + n, has_bias ? fmaf(a, ws, bias) : a * ws);
+          }
+      }
+    }
+  }
+}
+
+template <int W, int A, int MT>
+static cudaError_t launch_gemv_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
+                                 cudaStream_t stream) {
+  using C = GemvCfg<W, A, MT>;
+  const bool dots = p.dots != nullptr;
+  auto kernel = dots ? gemv_group64_kernel<W, A, MT, true> : gemv_group64_kernel<W, A, MT, false>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[2][64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dots][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured[dots][dev] = true;
+  }
+  kernel<<<(p.N + C::ROWS - 1) / C::ROWS, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
+                                cudaStream_t stream) {
+  const int mt = p.M <= 16 ? 1 : 2;
+#define ACTUNE_CASE(WW, AA)                                                      \
+  if (W == WW && A == AA)                                                        \
+    return mt == 1 ? launch_gemv_t<WW, AA, 1>(ta, tw, p, stream) : launch_gemv_t<WW, AA, 2>(ta, tw, p, stream);
+  ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
+  ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
+  ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
+#undef ACTUNE_CASE
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace actune

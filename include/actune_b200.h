@@ -56,7 +56,8 @@ typedef enum actune_dtype {
  * variants compute the identical fp32 chain, so their outputs are bit-identical.
  * BN*: token rows on the MMA M side (128 per tile), BN weight rows per tile, both
  * operands staged in shared memory.  WT*: weights-in-tensor-memory form, 128
- * weight rows per tile expanded straight into TMEM, WT tokens per tile. */
+ * weight rows per tile expanded straight into TMEM, WT tokens per tile.  GEMV:
+ * warp-level integer MMAs streaming 32 weight rows per CTA, for up to 32 tokens. */
 typedef enum actune_variant {
   ACTUNE_VARIANT_AUTO = 0,
   ACTUNE_VARIANT_BN32 = 1,
@@ -65,7 +66,8 @@ typedef enum actune_variant {
   ACTUNE_VARIANT_WT16 = 4,
   ACTUNE_VARIANT_WT32 = 5,
   ACTUNE_VARIANT_WT64 = 6,
-  ACTUNE_VARIANT_WT128 = 7
+  ACTUNE_VARIANT_WT128 = 7,
+  ACTUNE_VARIANT_GEMV = 8 /* weight-streaming kernel for M <= 32 (AUTO picks it there) */
 } actune_variant;
 
 /* Device error codes reported by actune_device_error(). */
@@ -157,6 +159,11 @@ int actune_device_error(int* code, int* site, int reset);
 
 /* ACTUNE_ABI_VERSION of the loaded library. */
 int actune_abi_version(void);
+
+/* The cudaError_t value behind the last ACTUNE_ERR_CUDA returned on the calling
+ * thread (0 if none), for diagnostics; the reference surfaces the same detail in
+ * its TORCH_CHECK / CUDA error messages. */
+int actune_last_cuda_error(void);
 
 #ifdef __cplusplus
 }
