@@ -215,7 +215,7 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
     p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
     p.out_dtype = out_dtype;
     p.out_vec_ok = 0;
-    return cuda_status(launch_gemv_group64(W, A, ta, tw, p, stream));
+    return cuda_status(launch_gemv_group64(W, A, ta, tw, p, g_devices[dev].num_sms, stream));
   }
   const bool wt = is_wt_variant(variant);
   const int bn = wt ? pick_wt(variant, M) : pick_bn(variant, M, N, g_devices[dev].num_sms);

@@ -73,6 +73,67 @@ __device__ __forceinline__ uint4 load_codes16(const uint8_t* tile, int rows, int
   }
 }
 
+// Per-lane offsets into a swizzled stage: for a lane reading row r (r mod 8 == gid)
+// the 16-byte chunk of group gl is c = C(gl) + cl(t) with C(gl) = (gl*8*BITS mod 128)/16
+// fixed at compile time and cl(t) = t*2*BITS/16 (the sum stays below 8), so
+// tbl[k] = (((k + cl) ^ gid) << 4) + (t*2*BITS mod 16) covers every group with one
+// table lookup at a constant index.
+template <int BITS>
+struct LaneSwz {
+  uint32_t tbl[8];
+  __device__ __forceinline__ LaneSwz(int gid, int t) {
+    const int u = t * 2 * BITS, cl = u >> 4, sub = u & 15;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tbl[k] = ((((k + cl) & 7) ^ gid) << 4) + sub;
+  }
+};
+
+// load_codes16 with the group index a compile-time constant and the lane part
+// precomputed: `rowbase` = tile + r * 128.
+template <int BITS, int ROWS_BOX, int GL>
+__device__ __forceinline__ uint4 load_codes16_c(const uint8_t* rowbase, const LaneSwz<BITS>& sw) {
+  constexpr int off = GL * 8 * BITS;
+  constexpr int blk = off >> 7, c0 = (off & 127) >> 4;
+  const uint8_t* addr = rowbase + blk * ROWS_BOX * 128 + sw.tbl[c0];
+  if constexpr (BITS == 8) {
+    return *reinterpret_cast<const uint4*>(addr);
+  } else if constexpr (BITS == 4) {
+    const uint2 v = *reinterpret_cast<const uint2*>(addr);
+    const uint2 lo = unpack_w4_word(v.x), hi = unpack_w4_word(v.y);
+    return make_uint4(lo.x, lo.y, hi.x, hi.y);
+  } else {
+    return unpack_w2_word(*reinterpret_cast<const uint32_t*>(addr));
+  }
+}
+
+// Exact int32 -> fp32 for |v| < 2^22 at full rate (see kMagicBits).
+__device__ __forceinline__ float exact_float(int32_t v) {
+  return __uint_as_float((uint32_t)v + kMagicBits) - kMagicValue;
+}
+
+template <int GL, int W, int A, bool DOTS, typename F>
+__device__ __forceinline__ void gemv2_group(const uint8_t* wrow, const uint8_t* arow_lo, const uint8_t* arow_hi,
+                                            const LaneSwz<W>& sww, const LaneSwz<A>& swa, F&& emit) {
+  const uint4 wq = load_codes16_c<W, 32, GL>(wrow, sww);
+  const uint4 a_lo = load_codes16_c<A, 16, GL>(arow_lo, swa);
+  const uint4 a_hi = load_codes16_c<A, 16, GL>(arow_hi, swa);
+  int32_t d[4] = {0, 0, 0, 0};
+  const uint32_t a0[4] = {a_lo.x, a_hi.x, a_lo.y, a_hi.y};
+  mma_s8_16832(d, a0, wq.x, wq.y);
+  const uint32_t a1[4] = {a_lo.z, a_hi.z, a_lo.w, a_hi.w};
+  mma_s8_16832(d, a1, wq.z, wq.w);
+  emit(GL, d);
+}
+
+template <int GL, int GPS, int W, int A, bool DOTS, typename F>
+__device__ __forceinline__ void gemv2_groups(const uint8_t* wrow, const uint8_t* arow_lo, const uint8_t* arow_hi,
+                                             const LaneSwz<W>& sww, const LaneSwz<A>& swa, F&& emit) {
+  if constexpr (GL < GPS) {
+    gemv2_group<GL, W, A, DOTS>(wrow, arow_lo, arow_hi, sww, swa, emit);
+    gemv2_groups<GL + 1, GPS, W, A, DOTS>(wrow, arow_lo, arow_hi, sww, swa, emit);
+  }
+}
+
 enum : int { kGvSiteProducer = 31, kGvSiteFull, kGvSiteDrain };
 
 template <int W, int A, int MT, bool DOTS>
@@ -266,6 +327,205 @@ __global__ void __launch_bounds__(128) gemv_group64_kernel(const __grid_constant
   }
 }
 
+// ---------------------------------------------------------------------------
+// Up to 16 tokens: K split across warps inside the CTA, persistent over row blocks.
+//
+// A CTA streams 32-row weight blocks (blockIdx.x, blockIdx.x + gridDim.x, ...)
+// through one TMA ring; a dedicated producer warp keeps it full across block
+// boundaries, so HBM latency is paid once per CTA rather than once per block.
+// 12 compute warps = 4 row groups (8 rows each) x 3 K-lanes: K-lane q takes ring
+// stages q, q+3, ... of the stream, so three 1024-wide K stages are multiplied at
+// once.  Each warp turns its stage's 16 group dots into exact fp32 values in
+// registers and frees the ring slot; the fp32 chain then runs stage by stage in K
+// order, each row group's accumulators passing from K-lane to K-lane through shared
+// memory (per row group and K-lane a barrier that completes once per stage it
+// chains; a waiter is never more than one phase ahead of it).
+template <int W, int A>
+struct Gemv2Cfg {
+  static constexpr int ROWS = 32, TOK = 16, KSTG = 1024, GPS = 16, QL = 3;
+  static constexpr int COMPUTE_WARPS = 4 * QL;  // 13 warps with the producer: at most 4 per scheduler
+  static constexpr int THREADS = 32 * (COMPUTE_WARPS + 1);
+  static constexpr int A_BLK = KSTG * A / 8 / 128;
+  static constexpr int W_BLK = KSTG * W / 8 / 128;
+  static constexpr int A_BYTES = A_BLK * TOK * 128;
+  static constexpr int W_BYTES = W_BLK * ROWS * 128;
+  static constexpr int STAGE_BYTES = (A_BYTES + W_BYTES + 1023) / 1024 * 1024;
+  static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+  static constexpr int SHIFT = (8 - A) + (8 - W);
+  static_assert(STAGES >= QL, "every K-lane needs a stage in flight");
+  static_assert(A_BLK + W_BLK <= 32, "one box per producer lane");
+};
+
+enum : int { kGv2SiteProducer = 41, kGv2SiteFull, kGv2SiteChain, kGv2SiteDrain };
+
+template <int W, int A, bool DOTS>
+__global__ void __launch_bounds__(Gemv2Cfg<W, A>::THREADS, 1)
+    gemv2_group64_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
+                         const GemmParams p) {
+  using C = Gemv2Cfg<W, A>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t chain_bar[4][C::QL];
+  __shared__ float4 acc_smem[4][32];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G;
+  const int n_stages = (G + C::GPS - 1) / C::GPS;
+  const int n_blocks = (p.N + C::ROWS - 1) / C::ROWS;
+  const int my_blocks = blockIdx.x < n_blocks ? (n_blocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int total = my_blocks * n_stages;  // stages this CTA streams
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 4);
+    }
+    for (int r = 0; r < 4; ++r)
+      for (int q = 0; q < C::QL; ++q) mbar_init(&chain_bar[r][q], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == C::COMPUTE_WARPS) {
+    // ---------------------------------------------------------------- producer
+    constexpr int NBOX = C::A_BLK + C::W_BLK;
+    constexpr uint32_t PMASK = (NBOX >= 32) ? 0xffffffffu : ((1u << NBOX) - 1u);
+    if (lane < NBOX) {
+      if (lane < 2) prefetch_tensormap(lane == 0 ? &tm_act : &tm_wgt);
+      int issued = 0;
+      for (int it = 0; it < total; ++it) {
+        const int s = it % C::STAGES;
+        const int rb = blockIdx.x + (it / n_stages) * gridDim.x, st = it % n_stages;
+        bool ok = true;
+        if (lane == 0) {
+          ok = mbar_wait(&empty_bar[s], ((it / C::STAGES) & 1) ^ 1, kGv2SiteProducer);
+          if (ok) mbar_arrive_expect_tx(&full_bar[s], C::A_BYTES + C::W_BYTES);
+        }
+        if (!__shfl_sync(PMASK, ok, 0)) break;
+        uint8_t* base = smem + s * C::STAGE_BYTES;
+        if (lane < C::A_BLK)
+          tma_load_2d(base + lane * C::TOK * 128, &tm_act, (st * C::A_BLK + lane) * 128, 0, &full_bar[s]);
+        else
+          tma_load_2d(base + C::A_BYTES + (lane - C::A_BLK) * C::ROWS * 128, &tm_wgt,
+                      (st * C::W_BLK + lane - C::A_BLK) * 128, rb * C::ROWS, &full_bar[s]);
+        ++issued;
+      }
+      // Never leave the CTA with bulk copies still landing in shared memory.
+      if (lane == 0) {
+        for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it)
+          mbar_wait(&full_bar[it % C::STAGES], (it / C::STAGES) & 1, kGv2SiteDrain);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ compute
+  const int r = warp & 3, q = warp >> 2;  // row group, K-lane (warps 4q .. 4q+3)
+  const int gid = lane >> 2, t = lane & 3;
+  const int row = r * 8 + gid;            // this lane's B-operand row within the block
+  const float shift_scale = 1.0f / float(1 << C::SHIFT);
+  const bool tok0 = gid < p.M, tok1 = gid + 8 < p.M;
+  const float* s0p = DOTS ? nullptr : p.act_scale + (int64_t)(tok0 ? gid : 0) * G;
+  const float* s1p = DOTS ? nullptr : p.act_scale + (int64_t)(tok1 ? gid + 8 : 0) * G;
+  const LaneSwz<W> sww(gid, t);
+  const LaneSwz<A> swa(gid, t);
+  for (int it = q; it < total; it += C::QL) {
+    const int s = it % C::STAGES;
+    const int rb = blockIdx.x + (it / n_stages) * gridDim.x, st = it % n_stages;
+    const int g0 = st * C::GPS;
+    // Scales of this stage (consumed by the chain below, fetched before the waits).
+    float sc0[C::GPS], sc1[C::GPS];
+#pragma unroll
+    for (int gl = 0; gl < C::GPS; ++gl) {
+      const int g = g0 + gl;
+      sc0[gl] = (!DOTS && tok0 && g < G) ? __ldg(s0p + g) * shift_scale : 0.f;
+      sc1[gl] = (!DOTS && tok1 && g < G) ? __ldg(s1p + g) * shift_scale : 0.f;
+    }
+    if (!mbar_wait(&full_bar[s], (it / C::STAGES) & 1, kGv2SiteFull)) break;
+    const uint8_t* a_tile = smem + s * C::STAGE_BYTES;
+    const uint8_t* w_tile = a_tile + C::A_BYTES;
+    float dots[C::GPS][4];
+    gemv2_groups<0, C::GPS, W, A, DOTS>(
+        w_tile + row * 128, a_tile + gid * 128, a_tile + (gid + 8) * 128, sww, swa, [&](int gl, const int32_t (&d)[4]) {
+          if constexpr (DOTS) {
+            const int g = g0 + gl;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int m = (i >> 1) * 8 + gid;
+              const int n = rb * C::ROWS + r * 8 + 2 * t + (i & 1);
+              if (m < p.M && n < p.N && g < G) p.dots[((int64_t)m * p.N + n) * G + g] = d[i] >> C::SHIFT;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dots[gl][i] = exact_float(d[i]);
+          }
+        });
+    // The ring slot is free as soon as every row group of this K-lane has its dots.
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);
+    if constexpr (!DOTS) {
+      // Chain: stage it - 1 (same row group, previous K-lane) must be folded in first.
+      // A block's first stage starts from zero but still waits, so that the stage
+      // before it has read the shared accumulator slot this stage will overwrite.
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (it != 0) {
+        const int qp = (q + C::QL - 1) % C::QL;
+        if (!mbar_wait(&chain_bar[r][qp], ((it - 1) / C::QL) & 1, kGv2SiteChain)) break;
+        if (st != 0) acc = acc_smem[r][lane];
+      }
+      // Groups past the end of K have dot 0 and scale 0: acc += 0 * 0 keeps acc.
+#pragma unroll
+      for (int gl = 0; gl < C::GPS; ++gl) {
+        acc.x = fmaf(dots[gl][0], sc0[gl], acc.x);
+        acc.y = fmaf(dots[gl][1], sc0[gl], acc.y);
+        acc.z = fmaf(dots[gl][2], sc1[gl], acc.z);
+        acc.w = fmaf(dots[gl][3], sc1[gl], acc.w);
+      }
+      if (st == n_stages - 1) {
+        const bool has_bias = p.bias_dtype != kDtNone;
+#pragma unroll
+        for (int i2 = 0; i2 < 2; ++i2) {
+          const int n = rb * C::ROWS + r * 8 + 2 * t + i2;
+          if (n >= p.N) continue;
+          const float ws = __ldg(p.w_scale + n);
+          const float bias = has_bias ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+          const float a0v = i2 ? acc.y : acc.x, a1v = i2 ? acc.w : acc.z;
+          if (tok0) store_scalar(p, (int64_t)gid * p.N + n, has_bias ? fmaf(a0v, ws, bias) : a0v * ws);
+          if (tok1) store_scalar(p, (int64_t)(gid + 8) * p.N + n, has_bias ? fmaf(a1v, ws, bias) : a1v * ws);
+        }
+      } else {
+        acc_smem[r][lane] = acc;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&chain_bar[r][q]);
+    }
+  }
+}
+
+template <int W, int A>
+static cudaError_t launch_gemv2_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, int num_sms,
+                                  cudaStream_t stream) {
+  using C = Gemv2Cfg<W, A>;
+  const bool dots = p.dots != nullptr;
+  auto kernel = dots ? gemv2_group64_kernel<W, A, true> : gemv2_group64_kernel<W, A, false>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[2][64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dots][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured[dots][dev] = true;
+  }
+  const int blocks = (p.N + C::ROWS - 1) / C::ROWS;
+  const int grid = blocks < num_sms ? blocks : num_sms;
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, p);
+  return cudaGetLastError();
+}
+
 template <int W, int A, int MT>
 static cudaError_t launch_gemv_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
                                  cudaStream_t stream) {
@@ -286,11 +546,10 @@ static cudaError_t launch_gemv_t(const CUtensorMap& ta, const CUtensorMap& tw, c
 }
 
 cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
-                                cudaStream_t stream) {
-  const int mt = p.M <= 16 ? 1 : 2;
+                                int num_sms, cudaStream_t stream) {
 #define ACTUNE_CASE(WW, AA)                                                      \
   if (W == WW && A == AA)                                                        \
-    return mt == 1 ? launch_gemv_t<WW, AA, 1>(ta, tw, p, stream) : launch_gemv_t<WW, AA, 2>(ta, tw, p, stream);
+    return p.M <= 16 ? launch_gemv2_t<WW, AA>(ta, tw, p, num_sms, stream) : launch_gemv_t<WW, AA, 2>(ta, tw, p, stream);
   ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
   ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
   ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)

@@ -101,6 +101,136 @@ __global__ void gated_act_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bflo
   }
 }
 
+// ---- vectorised forms (16-byte loads/stores); shapes must be multiples of 8 ----
+__device__ __forceinline__ void unpack8(const uint4 u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  return make_uint4(pack2(v[0], v[1]), pack2(v[2], v[3]), pack2(v[4], v[5]), pack2(v[6], v[7]));
+}
+__device__ __forceinline__ float bf16_round(float v) { return bf2f(__float2bfloat16_rn(v)); }
+
+// One CTA (256 threads) per row, CPT chunks of 8 elements per thread kept in
+// registers: D <= 2048 * CPT, D % 8 == 0.  Same arithmetic as rmsnorm_kernel.
+template <int CPT>
+__global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const __nv_bfloat16* __restrict__ residual,
+                                                          const __nv_bfloat16* __restrict__ weight,
+                                                          __nv_bfloat16* __restrict__ out,
+                                                          __nv_bfloat16* __restrict__ residual_out, int D, float eps,
+                                                          int gemma) {
+  __shared__ float red[8];
+  const int64_t base = (int64_t)blockIdx.x * D;
+  float v[CPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    const int i = (threadIdx.x + c * 256) * 8;
+    if (i < D) {
+      unpack8(__ldg(reinterpret_cast<const uint4*>(x + base + i)), v[c]);
+      if (residual) {
+        float r[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(residual + base + i)), r);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[c][k] = bf16_round(v[c][k] + r[k]);
+        *reinterpret_cast<uint4*>(residual_out + base + i) = pack8(v[c]);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss += v[c][k] * v[c][k];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)D + eps);
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    const int i = (threadIdx.x + c * 256) * 8;
+    if (i < D) {
+      float w[8], o[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(weight + i)), w);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = gemma ? v[c][k] * inv * (1.f + w[k]) : w[k] * bf16_round(v[c][k] * inv);
+      *reinterpret_cast<uint4*>(out + base + i) = pack8(o);
+    }
+  }
+}
+
+// Rotary embedding, one CTA per token; thread handles 8 consecutive rotation pairs
+// of one head (half % 8 == 0).
+__global__ void __launch_bounds__(256) rope_vec_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ cos_t,
+                                                       const float* __restrict__ sin_t, int Hq, int Hkv, int Dh) {
+  const int half = Dh / 2, per_head = half / 8, heads = Hq + Hkv;
+  const int t = blockIdx.x;
+  __nv_bfloat16* row = qkv + (int64_t)t * (Hq + 2 * Hkv) * Dh;
+  const float* cr = cos_t + (int64_t)t * half;
+  const float* sr = sin_t + (int64_t)t * half;
+  for (int item = threadIdx.x; item < heads * per_head; item += blockDim.x) {
+    const int h = item / per_head, j = (item % per_head) * 8;
+    __nv_bfloat16* b = row + h * Dh;
+    float a[8], bb[8], c[8], s[8];
+    unpack8(*reinterpret_cast<const uint4*>(b + j), a);
+    unpack8(*reinterpret_cast<const uint4*>(b + j + half), bb);
+    const float4 c0 = __ldg(reinterpret_cast<const float4*>(cr + j)), c1 = __ldg(reinterpret_cast<const float4*>(cr + j + 4));
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(sr + j)), s1 = __ldg(reinterpret_cast<const float4*>(sr + j + 4));
+    c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+    s[0] = s0.x; s[1] = s0.y; s[2] = s0.z; s[3] = s0.w; s[4] = s1.x; s[5] = s1.y; s[6] = s1.z; s[7] = s1.w;
+    float o1[8], o2[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      o1[k] = a[k] * c[k] - bb[k] * s[k];
+      o2[k] = bb[k] * c[k] + a[k] * s[k];
+    }
+    *reinterpret_cast<uint4*>(b + j) = pack8(o1);
+    *reinterpret_cast<uint4*>(b + j + half) = pack8(o2);
+  }
+}
+
+// Gated activation, 8 outputs per thread (I % 8 == 0).
+__global__ void __launch_bounds__(256) gated_act_vec_kernel(const __nv_bfloat16* __restrict__ gu,
+                                                            __nv_bfloat16* __restrict__ out, int T, int I, int gelu) {
+  const int per_row = I / 8;
+  const int64_t total = (int64_t)T * per_row;
+  for (int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; item < total;
+       item += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(item / per_row), c = (int)(item % per_row) * 8;
+    float g[8], u[8], o[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(gu + (int64_t)t * 2 * I + c)), g);
+    unpack8(__ldg(reinterpret_cast<const uint4*>(gu + (int64_t)t * 2 * I + I + c)), u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float a;
+      if (gelu) {
+        const float kk = 0.7978845608028654f;  // sqrt(2/pi)
+        a = 0.5f * g[k] * (1.f + tanhf(kk * (g[k] + 0.044715f * g[k] * g[k] * g[k])));
+      } else {
+        a = g[k] / (1.f + __expf(-g[k]));
+      }
+      o[k] = bf16_round(a) * u[k];
+    }
+    *reinterpret_cast<uint4*>(out + item * 8) = pack8(o);
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 int grid_for(int64_t n) {
   int64_t b = (n + 255) / 256;
   if (b > 148 * 16) b = 148 * 16;
@@ -117,6 +247,20 @@ int actune_harness_rmsnorm(const void* x, const void* residual, const void* weig
       (residual != nullptr && residual_out == nullptr))
     return ACTUNE_ERR_INVALID_VALUE;
   if (T == 0) return ACTUNE_OK;
+  const bool vec = D % 8 == 0 && D <= 8192 && aligned16(x) && aligned16(weight) && aligned16(out) &&
+                   (residual == nullptr || (aligned16(residual) && aligned16(residual_out)));
+  if (vec) {
+    const auto cs = reinterpret_cast<cudaStream_t>(stream);
+    const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+    const auto* rb = reinterpret_cast<const __nv_bfloat16*>(residual);
+    const auto* wb = reinterpret_cast<const __nv_bfloat16*>(weight);
+    auto* ob = reinterpret_cast<__nv_bfloat16*>(out);
+    auto* rob = reinterpret_cast<__nv_bfloat16*>(residual_out);
+    if (D <= 2048) rmsnorm_vec_kernel<1><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma);
+    else if (D <= 4096) rmsnorm_vec_kernel<2><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma);
+    else rmsnorm_vec_kernel<4><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma);
+    return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+  }
   rmsnorm_kernel<<<(unsigned)T, 256, D * sizeof(float), reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(residual),
       reinterpret_cast<const __nv_bfloat16*>(weight), reinterpret_cast<__nv_bfloat16*>(out),
@@ -129,6 +273,11 @@ int actune_harness_rope(void* qkv, const float* cos_t, const float* sin_t, int64
   if (T < 0 || Hq <= 0 || Hkv <= 0 || Dh <= 0 || Dh % 2 || qkv == nullptr || cos_t == nullptr || sin_t == nullptr)
     return ACTUNE_ERR_INVALID_VALUE;
   if (T == 0) return ACTUNE_OK;
+  if ((Dh / 2) % 8 == 0 && aligned16(qkv) && aligned16(cos_t) && aligned16(sin_t)) {
+    rope_vec_kernel<<<(unsigned)T, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<__nv_bfloat16*>(qkv), cos_t, sin_t, Hq, Hkv, Dh);
+    return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+  }
   const int64_t n = T * (Hq + Hkv) * (Dh / 2);
   rope_kernel<<<grid_for(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<__nv_bfloat16*>(qkv), cos_t, sin_t, (int)T, Hq, Hkv, Dh);
@@ -138,6 +287,11 @@ int actune_harness_rope(void* qkv, const float* cos_t, const float* sin_t, int64
 int actune_harness_gated_act(const void* gu, void* out, int64_t T, int64_t I, int gelu, void* stream) {
   if (T < 0 || I <= 0 || gu == nullptr || out == nullptr) return ACTUNE_ERR_INVALID_VALUE;
   if (T == 0) return ACTUNE_OK;
+  if (I % 8 == 0 && aligned16(gu) && aligned16(out)) {
+    gated_act_vec_kernel<<<grid_for(T * I / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(out), (int)T, (int)I, gelu);
+    return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+  }
   gated_act_kernel<<<grid_for(T * I), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(out), (int)T, (int)I, gelu);
   return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;

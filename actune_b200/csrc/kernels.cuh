@@ -18,7 +18,7 @@ cudaError_t launch_r4_refine(const void* w, int dtype, int64_t N, int64_t K, con
 constexpr int kGemvStageK = 1024;
 constexpr int kGemvRows = 32;
 cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
-                                cudaStream_t stream);
+                                int num_sms, cudaStream_t stream);
 cudaError_t launch_pack_rows(const int8_t* q, int64_t total_bytes, int bits, uint8_t* packed, int num_sms,
                              cudaStream_t stream);
 

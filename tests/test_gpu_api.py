@@ -258,30 +258,34 @@ def test_shared_activation_scope_reuses_quantization():
     assert len(calls) == 2
 
 
-def test_harness_glue_kernels():
+@pytest.mark.parametrize("d", [256, 260, 4096, 8192])  # vectorised forms (D % 8 == 0) and the general one
+def test_harness_glue_kernels(d):
     from actune_b200 import harness as H
     torch.manual_seed(8)
-    x = torch.randn(7, 256, device="cuda", dtype=torch.bfloat16)
-    r = torch.randn(7, 256, device="cuda", dtype=torch.bfloat16)
-    w = torch.randn(256, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(7, d, device="cuda", dtype=torch.bfloat16)
+    r = torch.randn(7, d, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(d, device="cuda", dtype=torch.bfloat16)
     out, res = H.rmsnorm(x, w, 1e-5, r)
     s = (x.float() + r.float()).bfloat16().float()
     ref = w * (s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-5)).bfloat16()
     assert torch.equal(res, s.bfloat16())
     assert float((out.float() - ref.float()).abs().max()) <= 2 ** -6 * float(ref.abs().max())
-    gu = torch.randn(5, 2 * 96, device="cuda", dtype=torch.bfloat16)
+    inter = d // 2 + 4  # multiple of 8 only for some d
+    gu = torch.randn(5, 2 * inter, device="cuda", dtype=torch.bfloat16)
     ga = H.gated_act(gu)
-    g, u = gu.float().split(96, -1)
+    g, u = gu.float().split(inter, -1)
     torch.testing.assert_close(ga.float(), (F.silu(g).bfloat16().float() * u), rtol=2e-2, atol=2e-2)
-    qkv = torch.randn(6, (2 + 2 * 1) * 16, device="cuda", dtype=torch.bfloat16)
-    cos, sin = H.rope_tables(6, 16, 10000.0, "cuda")
-    before = qkv.clone()
-    H.rope_(qkv, cos, sin, 2, 1, 16)
-    q = before[:, :32].view(6, 2, 16).float()
-    rot = torch.cat([q[..., :8] * cos[:, None] - q[..., 8:] * sin[:, None],
-                     q[..., 8:] * cos[:, None] + q[..., :8] * sin[:, None]], -1)
-    torch.testing.assert_close(qkv[:, :32].view(6, 2, 16).float(), rot, rtol=1e-2, atol=1e-2)
-    assert torch.equal(qkv[:, 48:], before[:, 48:])  # v untouched
+    for dh in (16, 128):
+        qkv = torch.randn(6, (2 + 2 * 1) * dh, device="cuda", dtype=torch.bfloat16)
+        cos, sin = H.rope_tables(6, dh, 10000.0, "cuda")
+        before = qkv.clone()
+        H.rope_(qkv, cos, sin, 2, 1, dh)
+        q = before[:, :2 * dh].view(6, 2, dh).float()
+        hd = dh // 2
+        rot = torch.cat([q[..., :hd] * cos[:, None] - q[..., hd:] * sin[:, None],
+                         q[..., hd:] * cos[:, None] + q[..., :hd] * sin[:, None]], -1)
+        torch.testing.assert_close(qkv[:, :2 * dh].view(6, 2, dh).float(), rot, rtol=1e-2, atol=1e-2)
+        assert torch.equal(qkv[:, 3 * dh:], before[:, 3 * dh:])  # v untouched
 
 
 def test_small_oft_backbone_graph_vs_eager():
