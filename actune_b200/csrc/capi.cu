@@ -109,6 +109,34 @@ int pick_wt(int variant, int64_t M) {
 
 bool is_wt_variant(int variant) { return variant >= ACTUNE_VARIANT_WT16 && variant <= ACTUNE_VARIANT_WT128; }
 
+// 3-D uint8 tensor map over a [rows, row_bytes] matrix (row_bytes a multiple of
+// 128) seen as (128-byte block, row, block index): a box of {128, box_rows,
+// box_blocks} lands as [block][row][128 B], 128-byte swizzled.
+int encode_map_blocks(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box_rows,
+                      int box_blocks) {
+  const cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(row_bytes / 128)};
+  const cuuint64_t strides[2] = {(cuuint64_t)row_bytes, 128};
+  const cuuint32_t box[3] = {128, (cuuint32_t)box_rows, (cuuint32_t)box_blocks};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
+// 2-D fp32 tensor map over a [rows, cols] row-major matrix (cols a multiple of 4),
+// no swizzle; boxes of {box_cols, box_rows}.
+int encode_map_f32(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(cols * 4)};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
 bool use_gemv(int variant, int64_t M) {
   return variant == ACTUNE_VARIANT_GEMV || (variant == ACTUNE_VARIANT_AUTO && M <= 32);
 }
@@ -196,11 +224,24 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   if (!aligned(a, 16) || !aligned(w, 16)) return ACTUNE_ERR_MISALIGNED;
   if (use_gemv(variant, M)) {
     if (M > 32) return ACTUNE_ERR_INVALID_VALUE;
-    CUtensorMap ta, tw;
+    CUtensorMap ta, tw, ts;
     const int tok = M <= 16 ? 16 : 32;
-    rc = encode_map(&ta, a, M, K * A / 8, 128, tok, Swz::B128);
-    if (rc != ACTUNE_OK) return rc;
-    rc = encode_map(&tw, w, N, K * W / 8, 128, kGemvRows, Swz::B128);
+    // Whole-stage boxes need 128-byte packed rows and, for the scale tile, 16-byte
+    // scale rows at a 16-byte aligned base.
+    const bool whole = M <= 16 && (K * A / 8) % 128 == 0 && (K * W / 8) % 128 == 0 &&
+                       (dots != nullptr || ((K / 64) % 4 == 0 && aligned(a_scale, 16)));
+    if (whole) {
+      rc = encode_map_blocks(&ta, a, M, K * A / 8, (int)M, kGemvStageK * A / 8 / 128);
+      if (rc != ACTUNE_OK) return rc;
+      rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, kGemvStageK * W / 8 / 128);
+      if (rc != ACTUNE_OK) return rc;
+      ts = ta;  // never read by the dots export
+      if (dots == nullptr) rc = encode_map_f32(&ts, a_scale, M, K / 64, 16, (int)M);
+    } else {
+      rc = encode_map(&ta, a, M, K * A / 8, 128, tok, Swz::B128);
+      if (rc != ACTUNE_OK) return rc;
+      rc = encode_map(&tw, w, N, K * W / 8, 128, kGemvRows, Swz::B128);
+    }
     if (rc != ACTUNE_OK) return rc;
     GemmParams p{};
     p.act_scale = a_scale;
@@ -215,7 +256,7 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
     p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
     p.out_dtype = out_dtype;
     p.out_vec_ok = 0;
-    return cuda_status(launch_gemv_group64(W, A, ta, tw, p, g_devices[dev].num_sms, stream));
+    return cuda_status(launch_gemv_group64(W, A, ta, tw, whole ? &ts : nullptr, p, g_devices[dev].num_sms, stream));
   }
   const bool wt = is_wt_variant(variant);
   const int bn = wt ? pick_wt(variant, M) : pick_bn(variant, M, N, g_devices[dev].num_sms);

@@ -54,6 +54,21 @@ __device__ __forceinline__ void mma_s8_16832(int32_t (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Sixteen codes at `addr` (2 * BITS packed bytes) as four int8x4 words in K order,
+// sub-byte codes placed in the top bits of each int8.
+template <int BITS>
+__device__ __forceinline__ uint4 load_codes16_at(const uint8_t* addr) {
+  if constexpr (BITS == 8) {
+    return *reinterpret_cast<const uint4*>(addr);
+  } else if constexpr (BITS == 4) {
+    const uint2 v = *reinterpret_cast<const uint2*>(addr);
+    const uint2 lo = unpack_w4_word(v.x), hi = unpack_w4_word(v.y);
+    return make_uint4(lo.x, lo.y, hi.x, hi.y);
+  } else {
+    return unpack_w2_word(*reinterpret_cast<const uint32_t*>(addr));
+  }
+}
+
 // Sixteen codes (lane t's part of 64-wide group g) of row r of a staged operand as
 // four int8x4 words in K order.  `rows` is the row count of one box; the stage holds
 // [block][row][128 B] with the 128-byte swizzle.
@@ -61,77 +76,12 @@ template <int BITS>
 __device__ __forceinline__ uint4 load_codes16(const uint8_t* tile, int rows, int r, int g, int t) {
   const int off = g * 8 * BITS + t * 2 * BITS;  // byte offset of the lane's codes within the stage row
   const int blk = off >> 7, c = (off >> 4) & 7, sub = off & 15;
-  const uint8_t* addr = tile + (blk * rows + r) * 128 + ((c ^ (r & 7)) << 4) + sub;
-  if constexpr (BITS == 8) {
-    return *reinterpret_cast<const uint4*>(addr);
-  } else if constexpr (BITS == 4) {
-    const uint2 v = *reinterpret_cast<const uint2*>(addr);
-    const uint2 lo = unpack_w4_word(v.x), hi = unpack_w4_word(v.y);
-    return make_uint4(lo.x, lo.y, hi.x, hi.y);
-  } else {
-    return unpack_w2_word(*reinterpret_cast<const uint32_t*>(addr));
-  }
-}
-
-// Per-lane offsets into a swizzled stage: for a lane reading row r (r mod 8 == gid)
-// the 16-byte chunk of group gl is c = C(gl) + cl(t) with C(gl) = (gl*8*BITS mod 128)/16
-// fixed at compile time and cl(t) = t*2*BITS/16 (the sum stays below 8), so
-// tbl[k] = (((k + cl) ^ gid) << 4) + (t*2*BITS mod 16) covers every group with one
-// table lookup at a constant index.
-template <int BITS>
-struct LaneSwz {
-  uint32_t tbl[8];
-  __device__ __forceinline__ LaneSwz(int gid, int t) {
-    const int u = t * 2 * BITS, cl = u >> 4, sub = u & 15;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) tbl[k] = ((((k + cl) & 7) ^ gid) << 4) + sub;
-  }
-};
-
-// load_codes16 with the group index a compile-time constant and the lane part
-// precomputed: `rowbase` = tile + r * 128.
-template <int BITS, int ROWS_BOX, int GL>
-__device__ __forceinline__ uint4 load_codes16_c(const uint8_t* rowbase, const LaneSwz<BITS>& sw) {
-  constexpr int off = GL * 8 * BITS;
-  constexpr int blk = off >> 7, c0 = (off & 127) >> 4;
-  const uint8_t* addr = rowbase + blk * ROWS_BOX * 128 + sw.tbl[c0];
-  if constexpr (BITS == 8) {
-    return *reinterpret_cast<const uint4*>(addr);
-  } else if constexpr (BITS == 4) {
-    const uint2 v = *reinterpret_cast<const uint2*>(addr);
-    const uint2 lo = unpack_w4_word(v.x), hi = unpack_w4_word(v.y);
-    return make_uint4(lo.x, lo.y, hi.x, hi.y);
-  } else {
-    return unpack_w2_word(*reinterpret_cast<const uint32_t*>(addr));
-  }
+  return load_codes16_at<BITS>(tile + (blk * rows + r) * 128 + ((c ^ (r & 7)) << 4) + sub);
 }
 
 // Exact int32 -> fp32 for |v| < 2^22 at full rate (see kMagicBits).
 __device__ __forceinline__ float exact_float(int32_t v) {
   return __uint_as_float((uint32_t)v + kMagicBits) - kMagicValue;
-}
-
-template <int GL, int W, int A, bool DOTS, typename F>
-__device__ __forceinline__ void gemv2_group(const uint8_t* wrow, const uint8_t* arow_lo, const uint8_t* arow_hi,
-                                            const LaneSwz<W>& sww, const LaneSwz<A>& swa, F&& emit) {
-  const uint4 wq = load_codes16_c<W, 32, GL>(wrow, sww);
-  const uint4 a_lo = load_codes16_c<A, 16, GL>(arow_lo, swa);
-  const uint4 a_hi = load_codes16_c<A, 16, GL>(arow_hi, swa);
-  int32_t d[4] = {0, 0, 0, 0};
-  const uint32_t a0[4] = {a_lo.x, a_hi.x, a_lo.y, a_hi.y};
-  mma_s8_16832(d, a0, wq.x, wq.y);
-  const uint32_t a1[4] = {a_lo.z, a_hi.z, a_lo.w, a_hi.w};
-  mma_s8_16832(d, a1, wq.z, wq.w);
-  emit(GL, d);
-}
-
-template <int GL, int GPS, int W, int A, bool DOTS, typename F>
-__device__ __forceinline__ void gemv2_groups(const uint8_t* wrow, const uint8_t* arow_lo, const uint8_t* arow_hi,
-                                             const LaneSwz<W>& sww, const LaneSwz<A>& swa, F&& emit) {
-  if constexpr (GL < GPS) {
-    gemv2_group<GL, W, A, DOTS>(wrow, arow_lo, arow_hi, sww, swa, emit);
-    gemv2_groups<GL + 1, GPS, W, A, DOTS>(wrow, arow_lo, arow_hi, sww, swa, emit);
-  }
 }
 
 enum : int { kGvSiteProducer = 31, kGvSiteFull, kGvSiteDrain };
@@ -328,189 +278,261 @@ __global__ void __launch_bounds__(128) gemv_group64_kernel(const __grid_constant
 }
 
 // ---------------------------------------------------------------------------
-// Up to 16 tokens: K split across warps inside the CTA, persistent over row blocks.
+// Up to 16 tokens, packed rows a multiple of 128 bytes: every warp of the CTA on
+// every stage, persistent over row blocks.
 //
 // A CTA streams 32-row weight blocks (blockIdx.x, blockIdx.x + gridDim.x, ...)
-// through one TMA ring; a dedicated producer warp keeps it full across block
-// boundaries, so HBM latency is paid once per CTA rather than once per block.
-// 12 compute warps = 4 row groups (8 rows each) x 3 K-lanes: K-lane q takes ring
-// stages q, q+3, ... of the stream, so three 1024-wide K stages are multiplied at
-// once.  Each warp turns its stage's 16 group dots into exact fp32 values in
-// registers and frees the ring slot; the fp32 chain then runs stage by stage in K
-// order, each row group's accumulators passing from K-lane to K-lane through shared
-// memory (per row group and K-lane a barrier that completes once per stage it
-// chains; a waiter is never more than one phase ahead of it).
-template <int W, int A>
-struct Gemv2Cfg {
-  static constexpr int ROWS = 32, TOK = 16, KSTG = 1024, GPS = 16, QL = 3;
-  static constexpr int COMPUTE_WARPS = 4 * QL;  // 13 warps with the producer: at most 4 per scheduler
-  static constexpr int THREADS = 32 * (COMPUTE_WARPS + 1);
+// through one TMA ring.  A stage is three boxes: the weight tile and the token tile
+// as 3-D boxes over (128-byte block, row, block index) views, landing as
+// [block][row][128 B] with the 128-byte swizzle, and the stage's activation scales
+// [token][16 groups] fp32.  The TMA unit spends a roughly fixed time per box, so a
+// few large boxes keep the ring full where many small ones starve it; token boxes
+// are exactly M rows high because zero-filled rows cost as much as loaded ones.
+// 4 * QL warps = 4 row groups (8 rows) x QL K-lanes; K-lane q multiplies groups
+// q*GPQ .. q*GPQ+GPQ-1 of every stage, so all warps work on each stage as soon as
+// it lands.  The fp32 chain runs group by group in K order: per row group the
+// accumulators pass K-lane 0 -> 1 -> ... -> QL-1 -> next stage's 0 through shared
+// memory (one barrier per row group and K-lane, completing once per stage; a waiter
+// is never more than one phase ahead).  Each warp computes the next stage's dots
+// before folding the current one into the chain, so a hand-off rarely has to
+// wait, and no step of a stage reads global memory.  A stage slot is refilled by
+// one warp (round robin) once all warps have released it.
+template <int W, int A, int QL>
+struct Gemv3Cfg {
+  static constexpr int ROWS = 32, TOK = 16, KSTG = 1024, GPS = 16, GPQ = GPS / QL;
+  static constexpr int WARPS = 4 * QL, THREADS = 32 * WARPS;
   static constexpr int A_BLK = KSTG * A / 8 / 128;
   static constexpr int W_BLK = KSTG * W / 8 / 128;
-  static constexpr int A_BYTES = A_BLK * TOK * 128;
-  static constexpr int W_BYTES = W_BLK * ROWS * 128;
-  static constexpr int STAGE_BYTES = (A_BYTES + W_BYTES + 1023) / 1024 * 1024;
+  static constexpr int W_BYTES = W_BLK * ROWS * 128;      // multiple of 4096: the token tile stays 1024-aligned
+  static constexpr int A_BYTES = A_BLK * TOK * 128;       // room for 16 token rows
+  static constexpr int SC_BYTES = TOK * GPS * 4;
+  static constexpr int STAGE_BYTES = (W_BYTES + A_BYTES + SC_BYTES + 1023) / 1024 * 1024;
   static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
   static constexpr int SHIFT = (8 - A) + (8 - W);
-  static_assert(STAGES >= QL, "every K-lane needs a stage in flight");
-  static_assert(A_BLK + W_BLK <= 32, "one box per producer lane");
+  static_assert(STAGES >= 2, "ring depth");
+  static_assert(GPQ * QL == GPS, "K-lanes split a stage evenly");
 };
 
-enum : int { kGv2SiteProducer = 41, kGv2SiteFull, kGv2SiteChain, kGv2SiteDrain };
+// Byte offset, within a stage tile of box_rows-high 128-byte lines laid out
+// [block][row] with the 128-byte swizzle, of lane t's 16 codes of group gl in row r.
+template <int BITS>
+__device__ __forceinline__ uint32_t swizzled_offset(int gl, int t, int r, int box_rows) {
+  const int off = gl * 8 * BITS + t * 2 * BITS;
+  const int blk = off >> 7, c = (off >> 4) & 7, sub = off & 15;
+  const int line = blk * box_rows + r;
+  return (uint32_t)(line * 128 + ((c ^ (line & 7)) << 4) + sub);
+}
 
-template <int W, int A, bool DOTS>
-__global__ void __launch_bounds__(Gemv2Cfg<W, A>::THREADS, 1)
-    gemv2_group64_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
-                         const GemmParams p) {
-  using C = Gemv2Cfg<W, A>;
+// K-lanes per row group of the whole-stage kernel (4 unless ACTUNE_GEMV_KLANES=2).
+static int gemv_klanes() {
+  static const int v = [] {
+    const char* e = getenv("ACTUNE_GEMV_KLANES");
+    return (e != nullptr && e[0] == '2') ? 2 : 4;
+  }();
+  return v;
+}
+
+enum : int { kGv3SiteFull = 51, kGv3SiteEmpty, kGv3SiteChain, kGv3SiteDrain };
+
+template <int W, int A, int QL, bool DOTS>
+__global__ void __launch_bounds__(Gemv3Cfg<W, A, QL>::THREADS, 1)
+    gemv3_group64_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
+                         const __grid_constant__ CUtensorMap tm_scale, const GemmParams p) {
+  using C = Gemv3Cfg<W, A, QL>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
-  __shared__ __align__(8) uint64_t chain_bar[4][C::QL];
+  __shared__ __align__(8) uint64_t chain_bar[4][QL];
   __shared__ float4 acc_smem[4][32];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = p.G;
+  if (warp == 0 && lane < 3) prefetch_tensormap(lane == 0 ? &tm_act : lane == 1 ? &tm_wgt : &tm_scale);
+  const int G = p.G, Mb = p.M;  // token boxes are M rows high (M <= 16)
   const int n_stages = (G + C::GPS - 1) / C::GPS;
   const int n_blocks = (p.N + C::ROWS - 1) / C::ROWS;
   const int my_blocks = blockIdx.x < n_blocks ? (n_blocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int total = my_blocks * n_stages;  // stages this CTA streams
+  const int total = my_blocks * n_stages;
+  const uint32_t stage_tx = C::W_BYTES + Mb * (C::A_BLK * 128 + (DOTS ? 0 : C::GPS * 4));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 4);
+      mbar_init(&empty_bar[s], C::WARPS);
     }
     for (int r = 0; r < 4; ++r)
-      for (int q = 0; q < C::QL; ++q) mbar_init(&chain_bar[r][q], 1);
+      for (int q = 0; q < QL; ++q) mbar_init(&chain_bar[r][q], 1);
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == C::COMPUTE_WARPS) {
-    // ---------------------------------------------------------------- producer
-    constexpr int NBOX = C::A_BLK + C::W_BLK;
-    constexpr uint32_t PMASK = (NBOX >= 32) ? 0xffffffffu : ((1u << NBOX) - 1u);
-    if (lane < NBOX) {
-      if (lane < 2) prefetch_tensormap(lane == 0 ? &tm_act : &tm_wgt);
-      int issued = 0;
-      for (int it = 0; it < total; ++it) {
-        const int s = it % C::STAGES;
-        const int rb = blockIdx.x + (it / n_stages) * gridDim.x, st = it % n_stages;
-        bool ok = true;
-        if (lane == 0) {
-          ok = mbar_wait(&empty_bar[s], ((it / C::STAGES) & 1) ^ 1, kGv2SiteProducer);
-          if (ok) mbar_arrive_expect_tx(&full_bar[s], C::A_BYTES + C::W_BYTES);
-        }
-        if (!__shfl_sync(PMASK, ok, 0)) break;
-        uint8_t* base = smem + s * C::STAGE_BYTES;
-        if (lane < C::A_BLK)
-          tma_load_2d(base + lane * C::TOK * 128, &tm_act, (st * C::A_BLK + lane) * 128, 0, &full_bar[s]);
-        else
-          tma_load_2d(base + C::A_BYTES + (lane - C::A_BLK) * C::ROWS * 128, &tm_wgt,
-                      (st * C::W_BLK + lane - C::A_BLK) * 128, rb * C::ROWS, &full_bar[s]);
-        ++issued;
-      }
-      // Never leave the CTA with bulk copies still landing in shared memory.
-      if (lane == 0) {
-        for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it)
-          mbar_wait(&full_bar[it % C::STAGES], (it / C::STAGES) & 1, kGv2SiteDrain);
-      }
-    }
-    return;
-  }
-
-  // ------------------------------------------------------------------ compute
-  const int r = warp & 3, q = warp >> 2;  // row group, K-lane (warps 4q .. 4q+3)
-  const int gid = lane >> 2, t = lane & 3;
-  const int row = r * 8 + gid;            // this lane's B-operand row within the block
-  const float shift_scale = 1.0f / float(1 << C::SHIFT);
-  const bool tok0 = gid < p.M, tok1 = gid + 8 < p.M;
-  const float* s0p = DOTS ? nullptr : p.act_scale + (int64_t)(tok0 ? gid : 0) * G;
-  const float* s1p = DOTS ? nullptr : p.act_scale + (int64_t)(tok1 ? gid + 8 : 0) * G;
-  const LaneSwz<W> sww(gid, t);
-  const LaneSwz<A> swa(gid, t);
-  for (int it = q; it < total; it += C::QL) {
+  // Lanes 0 (weights), 1 (tokens) and 2 (scales) of the calling warp load stage
+  // `it` into its slot.
+  auto issue = [&](int it) {
     const int s = it % C::STAGES;
     const int rb = blockIdx.x + (it / n_stages) * gridDim.x, st = it % n_stages;
-    const int g0 = st * C::GPS;
-    // Scales of this stage (consumed by the chain below, fetched before the waits).
-    float sc0[C::GPS], sc1[C::GPS];
+    if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], stage_tx);
+    __syncwarp(0x7u);
+    uint8_t* base = smem + s * C::STAGE_BYTES;
+    if (lane == 0) tma_load_3d(base, &tm_wgt, 0, rb * C::ROWS, st * C::W_BLK, &full_bar[s]);
+    else if (lane == 1) tma_load_3d(base + C::W_BYTES, &tm_act, 0, 0, st * C::A_BLK, &full_bar[s]);
+    else if (!DOTS) tma_load_2d(base + C::W_BYTES + C::A_BYTES, &tm_scale, st * C::GPS, 0, &full_bar[s]);
+  };
+  if (warp == 0 && lane < 3) {
+    for (int it = 0; it < total && it < C::STAGES; ++it) issue(it);
+  }
+
+  const int r = warp & 3, q = warp >> 2;  // row group, K-lane
+  const int gid = lane >> 2, t = lane & 3;
+  const float shift_scale = 1.0f / float(1 << C::SHIFT);
+  const bool tok0 = gid < Mb, tok1 = gid + 8 < Mb, hi = Mb > 8;
+  uint32_t ow[C::GPQ], oa_lo[C::GPQ], oa_hi[C::GPQ];
 #pragma unroll
-    for (int gl = 0; gl < C::GPS; ++gl) {
-      const int g = g0 + gl;
-      sc0[gl] = (!DOTS && tok0 && g < G) ? __ldg(s0p + g) * shift_scale : 0.f;
-      sc1[gl] = (!DOTS && tok1 && g < G) ? __ldg(s1p + g) * shift_scale : 0.f;
+  for (int j = 0; j < C::GPQ; ++j) {
+    ow[j] = swizzled_offset<W>(q * C::GPQ + j, t, r * 8 + gid, C::ROWS);
+    oa_lo[j] = swizzled_offset<A>(q * C::GPQ + j, t, gid, Mb);
+    oa_hi[j] = swizzled_offset<A>(q * C::GPQ + j, t, gid + 8, Mb);
+  }
+
+  bool ok = true;
+  // Dots of one stage for this warp's groups, exact fp32 (or the dots export), and
+  // the matching activation scales times 2^-SHIFT (0 for absent tokens and groups).
+  auto compute = [&](int it, float (&dots)[C::GPQ][4], float (&sc)[C::GPQ][2]) {
+    const int s = it % C::STAGES;
+    const int rb = blockIdx.x + (it / n_stages) * gridDim.x, st = it % n_stages;
+    if (!mbar_wait(&full_bar[s], (it / C::STAGES) & 1, kGv3SiteFull)) {
+      ok = false;
+      return;
     }
-    if (!mbar_wait(&full_bar[s], (it / C::STAGES) & 1, kGv2SiteFull)) break;
-    const uint8_t* a_tile = smem + s * C::STAGE_BYTES;
-    const uint8_t* w_tile = a_tile + C::A_BYTES;
-    float dots[C::GPS][4];
-    gemv2_groups<0, C::GPS, W, A, DOTS>(
-        w_tile + row * 128, a_tile + gid * 128, a_tile + (gid + 8) * 128, sww, swa, [&](int gl, const int32_t (&d)[4]) {
-          if constexpr (DOTS) {
-            const int g = g0 + gl;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int m = (i >> 1) * 8 + gid;
-              const int n = rb * C::ROWS + r * 8 + 2 * t + (i & 1);
-              if (m < p.M && n < p.N && g < G) p.dots[((int64_t)m * p.N + n) * G + g] = d[i] >> C::SHIFT;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dots[gl][i] = exact_float(d[i]);
-          }
-        });
-    // The ring slot is free as soon as every row group of this K-lane has its dots.
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[s]);
+    const uint8_t* w_tile = smem + s * C::STAGE_BYTES;
+    const uint8_t* a_tile = w_tile + C::W_BYTES;
     if constexpr (!DOTS) {
-      // Chain: stage it - 1 (same row group, previous K-lane) must be folded in first.
-      // A block's first stage starts from zero but still waits, so that the stage
-      // before it has read the shared accumulator slot this stage will overwrite.
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (it != 0) {
-        const int qp = (q + C::QL - 1) % C::QL;
-        if (!mbar_wait(&chain_bar[r][qp], ((it - 1) / C::QL) & 1, kGv2SiteChain)) break;
-        if (st != 0) acc = acc_smem[r][lane];
-      }
-      // Groups past the end of K have dot 0 and scale 0: acc += 0 * 0 keeps acc.
+      const float* sc_tile = reinterpret_cast<const float*>(a_tile + C::A_BYTES);
 #pragma unroll
-      for (int gl = 0; gl < C::GPS; ++gl) {
-        acc.x = fmaf(dots[gl][0], sc0[gl], acc.x);
-        acc.y = fmaf(dots[gl][1], sc0[gl], acc.y);
-        acc.z = fmaf(dots[gl][2], sc1[gl], acc.z);
-        acc.w = fmaf(dots[gl][3], sc1[gl], acc.w);
+      for (int j = 0; j < C::GPQ; ++j) {
+        sc[j][0] = tok0 ? sc_tile[gid * C::GPS + q * C::GPQ + j] * shift_scale : 0.f;
+        sc[j][1] = tok1 ? sc_tile[(gid + 8) * C::GPS + q * C::GPQ + j] * shift_scale : 0.f;
       }
-      if (st == n_stages - 1) {
-        const bool has_bias = p.bias_dtype != kDtNone;
+    }
 #pragma unroll
-        for (int i2 = 0; i2 < 2; ++i2) {
-          const int n = rb * C::ROWS + r * 8 + 2 * t + i2;
-          if (n >= p.N) continue;
-          const float ws = __ldg(p.w_scale + n);
-          const float bias = has_bias ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
-          const float a0v = i2 ? acc.y : acc.x, a1v = i2 ? acc.w : acc.z;
-          if (tok0) store_scalar(p, (int64_t)gid * p.N + n, has_bias ? fmaf(a0v, ws, bias) : a0v * ws);
-          if (tok1) store_scalar(p, (int64_t)(gid + 8) * p.N + n, has_bias ? fmaf(a1v, ws, bias) : a1v * ws);
+    for (int j = 0; j < C::GPQ; ++j) {
+      const uint4 wq = load_codes16_at<W>(w_tile + ow[j]);
+      const uint4 a_lo = load_codes16_at<A>(a_tile + oa_lo[j]);
+      const uint4 a_hi = hi ? load_codes16_at<A>(a_tile + oa_hi[j]) : make_uint4(0, 0, 0, 0);
+      int32_t d[4] = {0, 0, 0, 0};
+      const uint32_t a0[4] = {a_lo.x, a_hi.x, a_lo.y, a_hi.y};
+      mma_s8_16832(d, a0, wq.x, wq.y);
+      const uint32_t a1[4] = {a_lo.z, a_hi.z, a_lo.w, a_hi.w};
+      mma_s8_16832(d, a1, wq.z, wq.w);
+      if constexpr (DOTS) {
+        const int g = st * C::GPS + q * C::GPQ + j;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int m = (i >> 1) * 8 + gid;
+          const int n = rb * C::ROWS + r * 8 + 2 * t + (i & 1);
+          if (m < p.M && n < p.N && g < G) p.dots[((int64_t)m * p.N + n) * G + g] = d[i] >> C::SHIFT;
         }
       } else {
-        acc_smem[r][lane] = acc;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dots[j][i] = exact_float(d[i]);
       }
+    }
+    // Release the slot; the round-robin refiller waits for all warps, then loads
+    // stage it + STAGES into it.
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);
+    if (warp == it % C::WARPS && it + C::STAGES < total && lane < 3) {
+      bool w_ok = true;
+      if (lane == 0) w_ok = mbar_wait(&empty_bar[s], (it / C::STAGES) & 1, kGv3SiteEmpty);
+      if (__shfl_sync(0x7u, w_ok, 0)) issue(it + C::STAGES);
+      else ok = false;
+    }
+  };
+  // Weight scales and bias of the last K-lane's output rows, loaded when a block
+  // starts so that the block's last step issues no dependent global load.
+  const bool has_bias = p.bias_dtype != kDtNone;
+  float ws_pre[2] = {0.f, 0.f}, bias_pre[2] = {0.f, 0.f};
+  // Fold one stage's dots into the chain (K order: K-lane 0 .. QL-1, then the next stage).
+  auto chain = [&](int it, const float (&dots)[C::GPQ][4], const float (&sc)[C::GPQ][2]) {
+    const int rb = blockIdx.x + (it / n_stages) * gridDim.x, st = it % n_stages;
+    const bool last = q == QL - 1 && st == n_stages - 1;
+    if (q == QL - 1 && st == 0) {
+#pragma unroll
+      for (int i2 = 0; i2 < 2; ++i2) {
+        const int n = rb * C::ROWS + r * 8 + 2 * t + i2;
+        ws_pre[i2] = n < p.N ? __ldg(p.w_scale + n) : 0.f;
+        bias_pre[i2] = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+      }
+    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    // Every hand-off except the CTA's very first waits for its predecessor, also
+    // at a block's first stage (where it starts from zero), so that the shared
+    // accumulator slot has been read before it is overwritten.
+    if (q > 0 || it > 0) {
+      const int qp = (q + QL - 1) % QL;
+      const int prev = q > 0 ? it : it - 1;
+      if (!mbar_wait(&chain_bar[r][qp], prev & 1, kGv3SiteChain)) {
+        ok = false;
+        return;
+      }
+      if (q > 0 || st > 0) acc = acc_smem[r][lane];
+    }
+    // A block's last step only reads the slot: free it for the next block at once.
+    if (last) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&chain_bar[r][q]);
     }
+    // Groups past the end of K have dot 0 and scale 0: acc += 0 * 0 keeps acc.
+#pragma unroll
+    for (int j = 0; j < C::GPQ; ++j) {
+      acc.x = fmaf(dots[j][0], sc[j][0], acc.x);
+      acc.y = fmaf(dots[j][1], sc[j][0], acc.y);
+      acc.z = fmaf(dots[j][2], sc[j][1], acc.z);
+      acc.w = fmaf(dots[j][3], sc[j][1], acc.w);
+    }
+    if (last) {
+#pragma unroll
+      for (int i2 = 0; i2 < 2; ++i2) {
+        const int n = rb * C::ROWS + r * 8 + 2 * t + i2;
+        if (n >= p.N) continue;
+        const float ws = ws_pre[i2], bias = bias_pre[i2];
+        const float a0v = i2 ? acc.y : acc.x, a1v = i2 ? acc.w : acc.z;
+        if (tok0) store_scalar(p, (int64_t)gid * p.N + n, has_bias ? fmaf(a0v, ws, bias) : a0v * ws);
+        if (tok1) store_scalar(p, (int64_t)(gid + 8) * p.N + n, has_bias ? fmaf(a1v, ws, bias) : a1v * ws);
+      }
+    } else {
+      acc_smem[r][lane] = acc;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&chain_bar[r][q]);
+    }
+  };
+
+  float dots_a[C::GPQ][4], sc_a[C::GPQ][2], dots_b[C::GPQ][4], sc_b[C::GPQ][2];
+  if (total > 0) compute(0, dots_a, sc_a);
+  for (int it = 0; it < total && ok; it += 2) {
+    // Ping-pong register sets (constant indices keep them in registers).
+    if (it + 1 < total) compute(it + 1, dots_b, sc_b);
+    if (!ok) break;
+    if constexpr (!DOTS) chain(it, dots_a, sc_a);
+    if (!ok || it + 1 >= total) break;
+    if (it + 2 < total) compute(it + 2, dots_a, sc_a);
+    if (!ok) break;
+    if constexpr (!DOTS) chain(it + 1, dots_b, sc_b);
+  }
+  // Never leave the CTA with bulk copies still landing in shared memory.
+  if (warp == 0 && lane == 0) {
+    for (int it = total > C::STAGES ? total - C::STAGES : 0; it < total; ++it)
+      mbar_wait(&full_bar[it % C::STAGES], (it / C::STAGES) & 1, kGv3SiteDrain);
   }
 }
 
-template <int W, int A>
-static cudaError_t launch_gemv2_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, int num_sms,
-                                  cudaStream_t stream) {
-  using C = Gemv2Cfg<W, A>;
+template <int W, int A, int QL>
+static cudaError_t launch_gemv3_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
+                                  const GemmParams& p, int num_sms, cudaStream_t stream) {
+  using C = Gemv3Cfg<W, A, QL>;
   const bool dots = p.dots != nullptr;
-  auto kernel = dots ? gemv2_group64_kernel<W, A, true> : gemv2_group64_kernel<W, A, false>;
+  auto kernel = dots ? gemv3_group64_kernel<W, A, QL, true> : gemv3_group64_kernel<W, A, QL, false>;
   int dev = 0;
   cudaGetDevice(&dev);
   static bool configured[2][64] = {};
@@ -522,7 +544,7 @@ static cudaError_t launch_gemv2_t(const CUtensorMap& ta, const CUtensorMap& tw, 
   }
   const int blocks = (p.N + C::ROWS - 1) / C::ROWS;
   const int grid = blocks < num_sms ? blocks : num_sms;
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, p);
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, ts, p);
   return cudaGetLastError();
 }
 
@@ -545,11 +567,16 @@ static cudaError_t launch_gemv_t(const CUtensorMap& ta, const CUtensorMap& tw, c
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
-                                int num_sms, cudaStream_t stream) {
-#define ACTUNE_CASE(WW, AA)                                                      \
-  if (W == WW && A == AA)                                                        \
-    return p.M <= 16 ? launch_gemv2_t<WW, AA>(ta, tw, p, num_sms, stream) : launch_gemv_t<WW, AA, 2>(ta, tw, p, stream);
+cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap* ts,
+                                const GemmParams& p, int num_sms, cudaStream_t stream) {
+  const int ql = gemv_klanes();
+#define ACTUNE_CASE(WW, AA)                                                                                  \
+  if (W == WW && A == AA) {                                                                                  \
+    if (ts != nullptr)                                                                                       \
+      return ql == 2 ? launch_gemv3_t<WW, AA, 2>(ta, tw, *ts, p, num_sms, stream)                            \
+                     : launch_gemv3_t<WW, AA, 4>(ta, tw, *ts, p, num_sms, stream);                           \
+    return p.M <= 16 ? launch_gemv_t<WW, AA, 1>(ta, tw, p, stream) : launch_gemv_t<WW, AA, 2>(ta, tw, p, stream); \
+  }
   ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
   ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
   ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)

@@ -12,13 +12,16 @@ cudaError_t launch_weight_codes(const void* w, int dtype, int64_t N, int64_t K, 
                                 int8_t* codes, float* scale, cudaStream_t stream);
 cudaError_t launch_r4_refine(const void* w, int dtype, int64_t N, int64_t K, const int8_t* q4, const float* scale4,
                              int8_t* residual, int8_t* q8, cudaStream_t stream);
-// Weight-streaming kernel for M <= 32 (gemv_group64.cu).  Tensor maps: 2-D views
-// of the packed operands with 128-byte-wide, 128-byte-swizzled boxes of
-// 16 * ceil(M / 16) token rows and 32 weight rows.
+// Weight-streaming kernels for M <= 32 (gemv_group64.cu).  With `ts` (M <= 16, packed
+// rows a multiple of 128 bytes): 3-D maps over (128-byte block, row, block index) with
+// boxes of {128, M, 8 * A} tokens and {128, 32, 8 * W} weight rows, and `ts` a 2-D fp32
+// map over the activation scales with boxes of {16, M} (unused when p.dots is set).
+// Without: 2-D maps with 128-byte-wide boxes of 16 * ceil(M / 16) token rows and 32
+// weight rows.  Packed boxes use the 128-byte swizzle.
 constexpr int kGemvStageK = 1024;
 constexpr int kGemvRows = 32;
-cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
-                                int num_sms, cudaStream_t stream);
+cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap* ts,
+                                const GemmParams& p, int num_sms, cudaStream_t stream);
 cudaError_t launch_pack_rows(const int8_t* q, int64_t total_bytes, int bits, uint8_t* packed, int num_sms,
                              cudaStream_t stream);
 

@@ -139,7 +139,9 @@ def test_gemm_golden(ops, gemm_golden, w, a, si):
     pw = torch.from_numpy(g[f"{key}_pw"]).to(DEV)
     ws = torch.from_numpy(g[f"{key}_ws"]).to(DEV)
     bias = f32_of_bits(g[f"s{si}_bias"]).to(DEV)
-    for variant in range(8):  # AUTO, BN32/64/128 and the weights-in-TMEM WT16/32/64/128
+    # AUTO, BN32/64/128, the weights-in-TMEM WT16/32/64/128 and (M <= 32) the
+    # weight-streaming kernel.
+    for variant in range(9 if m <= 32 else 8):
         dots = ops.packed_linear_dots(pa, pw, k, w, a, variant=variant).cpu().numpy()
         ref = g[f"{key}_dots"]
         assert np.array_equal(dots[: ref.shape[0]], ref), f"dots variant {variant}"
@@ -191,6 +193,29 @@ def test_gemm_weights_in_tmem_variants(ops, w, a, variant):
     for m, k, n in [(37, 448, 200), (130, 1024, 136)]:
         y, ref, _ = _case(ops, m, k, n, w, a, seed=m + k + n + variant, variant=variant)
         assert_bits(bf16_bits(y), O.to_bf16_bits(ref), f"bf16 output m={m} k={k} n={n}")
+
+
+DECODE_SHAPES = [
+    (1, 1536, 200),   # whole-stage boxes, partial last stage, ragged N
+    (5, 3072, 4800),  # whole-stage boxes, more 32-row blocks than SMs (persistent loop)
+    (16, 512, 96),    # whole-stage boxes, half a stage: K-lanes 2 and 3 see only padding
+    (3, 448, 72),     # packed rows not a multiple of 128 bytes: 2-D boxes
+    (24, 4096, 136),  # 17..32 tokens
+    (32, 1024, 64),
+]
+
+
+@pytest.mark.parametrize("w,a", PAIRS)
+@pytest.mark.parametrize("m,k,n", DECODE_SHAPES)
+def test_gemm_weight_streaming_variant(ops, w, a, m, k, n):
+    """The weight-streaming kernels (VARIANT_GEMV, and AUTO at M <= 32): fp32 output
+    bit-exact, per-group dots equal to the oracle's."""
+    y, ref, (pa, pw, pa_h) = _case(ops, m, k, n, w, a, seed=m + k + n + w * a, out_dtype=torch.float32,
+                                   variant=8)
+    assert_bits(y.numpy(), ref, f"fp32 output m={m} k={k} n={n}")
+    dots = ops.packed_linear_dots(pa, pw, k, w, a, variant=8).cpu().numpy()
+    assert np.array_equal(dots, O.group_dots(pa_h, pw.cpu().numpy(), k, w, a))
+    assert torch.equal(ops.packed_linear_dots(pa, pw, k, w, a, variant=0).cpu(), torch.from_numpy(dots))
 
 
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
