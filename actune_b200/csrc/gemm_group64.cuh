@@ -16,10 +16,10 @@
 //   warp 0      TMA producer: packed activation and weight tiles -> smem ring
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer (straight-line
 //               4 MMAs per stage from precomputed descriptors)
-//   warps 2-3   converters: sub-byte codes -> int8 in the canonical
+//   warps 2-5   converters (sub-byte W or A only): codes -> int8 in the canonical
 //               128B-swizzled K-major layout (code placed in the top bits of
 //               the byte, i.e. scaled by 2^(8-bits); compensated exactly in fp32)
-//   warps 4-11  epilogue: tcgen05.ld of each group's int32 dots, exact
+//   then 8      epilogue warps: tcgen05.ld of each group's int32 dots, exact
 //               int->fp32 conversion, packed fp32x2 FMA into register
 //               accumulators, final scale/bias/convert/store
 #pragma once
@@ -54,10 +54,13 @@ struct Group64Cfg {
   static constexpr int KS = 128;     // K elements per pipeline stage (two groups)
   static constexpr int EPI_WG = 2;   // two epilogue warpgroups split the columns
   static constexpr int COLS = BN / EPI_WG;      // accumulator columns per epilogue thread
-  static constexpr int THREADS = 128 + 128 * EPI_WG;
   static constexpr int NPAIR = BN == 32 ? 4 : 2;   // accumulator buffer pairs (one pair per stage)
   static constexpr int TMEM_COLS = NPAIR * 2 * BN; // 256 or 512 (power of two)
   static constexpr bool CONVERT = (A < 8) || (W < 8);
+  // Warps: producer, MMA issuer, CVT_WARPS converters, then 4 * EPI_WG epilogue warps.
+  static constexpr int CVT_WARPS = CONVERT ? 4 : 0;
+  static constexpr int EPI_WARP0 = 2 + CVT_WARPS;
+  static constexpr int THREADS = 32 * EPI_WARP0 + 128 * EPI_WG;
   // Per-stage shared-memory layout: [act int8 | wgt int8 | act packed | wgt packed].
   static constexpr int OP_A_BYTES = BM * KS;        // 16 KB, SW128 K-major
   static constexpr int OP_W_BYTES = BN * KS;
@@ -84,12 +87,14 @@ struct Group64Cfg {
 // items; thread t handles items t, t + NT, ... which all share the same chunk
 // index and row phase (r mod 8), so every address is a per-thread base plus a
 // compile-time offset.
-template <int BITS, int ROWS, int NT>
+template <int BITS, int ROWS, int NT_ALL>
 __device__ __forceinline__ void unpack_stage(const uint8_t* __restrict__ stg, uint8_t* __restrict__ op, int tid) {
   constexpr int IPR = BITS;                   // items per row: 16*BITS packed bytes / 16
   constexpr int CHUNKS = 8 / IPR;             // output chunks per item
   constexpr int ITEMS = ROWS * IPR;
+  constexpr int NT = NT_ALL < ITEMS ? NT_ALL : ITEMS;  // threads with work
   static_assert(ITEMS % NT == 0, "items must split evenly");
+  if (tid >= NT) return;
   constexpr int ROW_STEP = NT / IPR;          // rows advanced per pass
   static_assert(ROW_STEP % 8 == 0, "row step must keep the swizzle phase");
   const int r0 = tid / IPR, i = tid % IPR;
@@ -196,7 +201,7 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_raw[s], 1);
-      mbar_init(&full_op[s], 2);
+      mbar_init(&full_op[s], C::CVT_WARPS > 0 ? C::CVT_WARPS : 1);  // one arrival per converter warp
       mbar_init(&empty_bar[s], 1);
     }
     for (int b = 0; b < C::NPAIR; ++b) {
@@ -336,17 +341,18 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
       mma_commit(&mma_done);
       mbar_wait(&mma_done, 0, kSiteMmaDone);
     }
-  } else if (warp < 4) {
+  } else if (warp < C::EPI_WARP0) {
     // ------------------------------------------------------------ converters
     if constexpr (C::CONVERT) {
       const int ctid = threadIdx.x - 64;
+      constexpr int NT = 32 * C::CVT_WARPS;
       for (int it = 0; it < n_iters; ++it) {
         const int s = it % C::STAGES;
         if (!mbar_wait(&full_raw[s], (it / C::STAGES) & 1, kSiteConverter)) break;
         uint8_t* st = smem + s * C::STAGE_BYTES;
-        if constexpr (A < 8) unpack_stage<A, C::BM, 64>(st + C::OP_A_BYTES + C::OP_W_BYTES, st, ctid);
+        if constexpr (A < 8) unpack_stage<A, C::BM, NT>(st + C::OP_A_BYTES + C::OP_W_BYTES, st, ctid);
         if constexpr (W < 8)
-          unpack_stage<W, BN, 64>(st + C::OP_A_BYTES + C::OP_W_BYTES + C::STG_A_BYTES, st + C::OP_A_BYTES, ctid);
+          unpack_stage<W, BN, NT>(st + C::OP_A_BYTES + C::OP_W_BYTES + C::STG_A_BYTES, st + C::OP_A_BYTES, ctid);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full_op[s]);
@@ -359,14 +365,17 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
     // accumulation of the previous half, and the first half of the next stage
     // is loaded before the last half of this one is accumulated.  Activation
     // scales are fetched two stages ahead into static register slots.
-    const int ew = warp - 4;
-    const int q = ew & 3;        // TMEM lane quarter this warp may access
+    const int ew = warp - C::EPI_WARP0;
+    const int q = warp & 3;      // TMEM lane quarter this warp may access
     const int e = ew >> 2;       // column slice
     const int row = q * 32 + lane;
     const int m = m0 + row;
     const bool warp_live = (m0 + q * 32) < p.M;  // any valid token row in this warp
     const int col0 = n0 + e * C::COLS;
-    constexpr int H = C::COLS / 2;
+    // TMEM is read in P parts of H columns per group: quarters when converter warps
+    // share the register file, halves otherwise.
+    constexpr int P = C::CVT_WARPS > 0 && C::COLS >= 16 ? 4 : 2;
+    constexpr int H = C::COLS / P;
     const float shift_scale = 1.0f / float(1 << C::SHIFT);
     const bool load_scales = !DOTS && warp_live && m < p.M;
     const float* as_row = p.act_scale + (int64_t)(m < p.M ? m : 0) * G;
@@ -397,7 +406,11 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
         tmem_ld<H>(lane_base, ra);
         tmem_wait_ld();
       }
-      // One stage: ra already holds (group 2it, first half).
+      // One stage: ra already holds part 0 of group 2it.  The 2 * P parts of the
+      // stage's two groups are read in order into ra / rb alternately, each load
+      // overlapping the accumulation of the part before it; the accumulator pair
+      // is released as soon as its last part is in registers, and part 0 of the
+      // next stage is loaded before that last part is accumulated.
       auto stage = [&](int it, float s0raw, float s1raw) {
         const int pr = it % C::NPAIR;
         const uint32_t base = lane_base + pr * (2 * BN);
@@ -406,33 +419,33 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
         // (scale_at), so acc += 0 * 0 leaves every accumulator unchanged (an
         // accumulator is never -0: it starts at +0 and the scales are > 0).
         const float s0 = s0raw * shift_scale, s1 = s1raw * shift_scale;
-        tmem_ld<H>(base + H, rb);
-        if constexpr (DOTS) store_dots<H>(p, m, col0, g0, ra, C::SHIFT);
-        else accumulate<H>(acc, ra, s0);
-        tmem_wait_ld();
-        tmem_ld<H>(base + BN, ra);
-        if constexpr (DOTS) store_dots<H>(p, m, col0 + H, g0, rb, C::SHIFT);
-        else accumulate<H>(acc + H / 2, rb, s0);
-        tmem_wait_ld();
-        tmem_ld<H>(base + BN + H, rb);
-        if constexpr (DOTS) store_dots<H>(p, m, col0, g0 + 1, ra, C::SHIFT);
-        else accumulate<H>(acc, ra, s1);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[pr]);
-        if (it + 1 < n_iters) {
-          const int pn = (it + 1) % C::NPAIR;
-          if (!mbar_wait(&acc_full[pn], ((it + 1) / C::NPAIR) & 1, kSiteEpilogue)) {
-            ok = false;
+        auto part_step = [&](int idx, uint32_t(&cur)[H], uint32_t(&nxt)[H]) {
+          const int grp = idx / P, part = idx % P;
+          if (idx + 1 < 2 * P) {
+            tmem_ld<H>(base + ((idx + 1) / P) * BN + ((idx + 1) % P) * H, nxt);
           } else {
-            tc_fence_after();
-            tmem_ld<H>(lane_base + pn * (2 * BN), ra);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[pr]);
+            if (it + 1 < n_iters) {
+              const int pn = (it + 1) % C::NPAIR;
+              if (!mbar_wait(&acc_full[pn], ((it + 1) / C::NPAIR) & 1, kSiteEpilogue)) {
+                ok = false;
+              } else {
+                tc_fence_after();
+                tmem_ld<H>(lane_base + pn * (2 * BN), nxt);
+              }
+            }
           }
+          if constexpr (DOTS) store_dots<H>(p, m, col0 + part * H, g0 + grp, cur, C::SHIFT);
+          else accumulate<H>(acc + part * (H / 2), cur, grp ? s1 : s0);
+          tmem_wait_ld();
+        };
+#pragma unroll
+        for (int idx = 0; idx < 2 * P; idx += 2) {
+          part_step(idx, ra, rb);
+          part_step(idx + 1, rb, ra);
         }
-        if constexpr (DOTS) store_dots<H>(p, m, col0 + H, g0 + 1, rb, C::SHIFT);
-        else accumulate<H>(acc + H / 2, rb, s1);
-        tmem_wait_ld();
       };
       // Scale slots: x for even stages, y for odd stages (fetched two stages ahead).
       float x0 = scale_at(0), x1 = scale_at(1), y0 = scale_at(2), y1 = scale_at(3);
@@ -463,7 +476,7 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
       }
       named_barrier_sync(1, 128 * C::EPI_WG);
       if (ok) {
-        const int et = threadIdx.x - 128;
+        const int et = threadIdx.x - 32 * C::EPI_WARP0;
         const int rows_here = min(C::BM, p.M - m0);
         for (int chunk = et; chunk < rows_here * (BN / 8); chunk += 128 * C::EPI_WG) {
           const int r = chunk / (BN / 8), c8 = (chunk % (BN / 8)) * 8;
