@@ -277,44 +277,6 @@ __global__ void __launch_bounds__(128) gemv_group64_kernel(const __grid_constant
   }
 }
 
-// ---------------------------------------------------------------------------
-// Up to 16 tokens, packed rows a multiple of 128 bytes: every warp of the CTA on
-// every stage, persistent over row blocks.
-//
-// A CTA streams 32-row weight blocks (blockIdx.x, blockIdx.x + gridDim.x, ...)
-// through one TMA ring.  A stage is three boxes: the weight tile and the token tile
-// as 3-D boxes over (128-byte block, row, block index) views, landing as
-// [block][row][128 B] with the 128-byte swizzle, and the stage's activation scales
-// [token][16 groups] fp32.  The TMA unit spends a roughly fixed time per box, so a
-// few large boxes keep the ring full where many small ones starve it; token boxes
-// are exactly M rows high because zero-filled rows cost as much as loaded ones.
-// 4 * QL warps = 4 row groups (8 rows) x QL K-lanes; K-lane q multiplies groups
-// q*GPQ .. q*GPQ+GPQ-1 of every stage, so all warps work on each stage as soon as
-// it lands.  The fp32 chain runs group by group in K order: per row group the
-// accumulators pass K-lane 0 -> 1 -> ... -> QL-1 -> next stage's 0 through shared
-// memory (one barrier per row group and K-lane, completing once per stage; a waiter
-// is never more than one phase ahead).  Each warp computes the next stage's dots
-// before folding the current one into the chain, so a hand-off rarely has to
-// wait, and no step of a stage reads global memory.  A stage slot is refilled by
-// one warp (round robin) once all warps have released it.
-template <int W, int A, int QL>
-struct Gemv3Cfg {
-  static constexpr int ROWS = 32, TOK = 16, KSTG = 1024, GPS = 16, GPQ = GPS / QL;
-  static constexpr int WARPS = 4 * QL, THREADS = 32 * WARPS;
-  static constexpr int A_BLK = KSTG * A / 8 / 128;
-  static constexpr int W_BLK = KSTG * W / 8 / 128;
-  static constexpr int W_BYTES = W_BLK * ROWS * 128;      // multiple of 4096: the token tile stays 1024-aligned
-  static constexpr int A_BYTES = A_BLK * TOK * 128;       // room for 16 token rows
-  static constexpr int SC_BYTES = TOK * GPS * 4;
-  static constexpr int STAGE_BYTES = (W_BYTES + A_BYTES + SC_BYTES + 1023) / 1024 * 1024;
-  static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
-  static constexpr int SHIFT = (8 - A) + (8 - W);
-  static_assert(STAGES >= 2, "ring depth");
-  static_assert(GPQ * QL == GPS, "K-lanes split a stage evenly");
-};
-
 // Byte offset, within a stage tile of box_rows-high 128-byte lines laid out
 // [block][row] with the 128-byte swizzle, of lane t's 16 codes of group gl in row r.
 template <int BITS>
@@ -325,214 +287,250 @@ __device__ __forceinline__ uint32_t swizzled_offset(int gl, int t, int r, int bo
   return (uint32_t)(line * 128 + ((c ^ (line & 7)) << 4) + sub);
 }
 
-// K-lanes per row group of the whole-stage kernel (4 unless ACTUNE_GEMV_KLANES=2).
-static int gemv_klanes() {
-  static const int v = [] {
-    const char* e = getenv("ACTUNE_GEMV_KLANES");
-    return (e != nullptr && e[0] == '2') ? 2 : 4;
-  }();
-  return v;
-}
+// ---------------------------------------------------------------------------
+// Up to 16 tokens, packed rows a multiple of 128 bytes: separate producer, dot and
+// chain roles, persistent over row blocks.
+//
+// A CTA streams 32-row weight blocks (blockIdx.x, blockIdx.x + gridDim.x, ...)
+// through one TMA ring.  A stage is K=1024 and three boxes: the weight tile and the
+// token tile as 3-D boxes over (128-byte block, row, block index) views, landing as
+// [block][row][128 B] with the 128-byte swizzle, and the stage's activation scales
+// [M][16] fp32.  The TMA unit spends a roughly fixed time per box, so a few large
+// boxes keep the ring full where many small ones starve it; token boxes are exactly
+// M rows high because zero-filled box rows cost as much as loaded ones.
+// One producer warp only issues copies.  16 dot warps = 2 row groups (16 weight
+// rows, two 8-row MMA column blocks sharing each token fragment) x 8 K-lanes
+// (K-lane q taking groups 2q, 2q+1 of every stage) turn a stage into exact fp32
+// dots and write them to a ring of dot buffers in shared memory; they never wait
+// for the fp32 chain except for a free dot buffer.  4 chain warps (one per 8 weight
+// rows) fold the dots into the chain in K order, fma(dot, scale, acc) group by
+// group, reading the scales from the stage slot, and write the outputs at the end
+// of a row block.  With at most 8 tokens only the real half of each dot fragment
+// is stored and read.  Shared-memory traffic per stage is what bounds this kernel
+// (the copies, the token fragments and the dot round trip share 128 B/clk).
+// A stage slot is free once the 16 dot warps and the 4 chain warps released it.
+template <int W, int A>
+struct Gemv4Cfg {
+  static constexpr int ROWS = 32, TOK = 16, KSTG = 1024, GPS = 16, QL = 8, GPQ = GPS / QL;
+  static constexpr int DOT_WARPS = 16, CHAIN_WARPS = 4, PRODUCER = DOT_WARPS + CHAIN_WARPS;
+  static constexpr int THREADS = 32 * (PRODUCER + 1);
+  static constexpr int A_BLK = KSTG * A / 8 / 128;
+  static constexpr int W_BLK = KSTG * W / 8 / 128;
+  static constexpr int W_BYTES = W_BLK * ROWS * 128;  // multiple of 4096
+  static constexpr int A_BYTES = A_BLK * TOK * 128;
+  static constexpr int SC_BYTES = TOK * GPS * 4;
+  static constexpr int STAGE_BYTES = (W_BYTES + A_BYTES + SC_BYTES + 1023) / 1024 * 1024;
+  // Dot buffers: [8-row block (4)][group of the stage][lane] float4 (lane's d0..d3).
+  static constexpr int DOT_BYTES = 4 * GPS * 32 * 16;  // 32 KB
+  static constexpr int DSTAGES = 2;
+  static constexpr int RING_BUDGET = 224 * 1024 - DSTAGES * DOT_BYTES;  // 227 KB per CTA at most
+  static constexpr int STAGES_FIT = RING_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + DSTAGES * DOT_BYTES + 1024;
+  static constexpr int SHIFT = (8 - A) + (8 - W);
+  static_assert(STAGES >= 2, "ring depth");
+};
 
-enum : int { kGv3SiteFull = 51, kGv3SiteEmpty, kGv3SiteChain, kGv3SiteDrain };
+enum : int { kGv4SiteFull = 61, kGv4SiteEmpty, kGv4SiteDotFull, kGv4SiteDotEmpty, kGv4SiteDrain };
 
-template <int W, int A, int QL, bool DOTS>
-__global__ void __launch_bounds__(Gemv3Cfg<W, A, QL>::THREADS, 1)
-    gemv3_group64_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
+template <int W, int A, bool DOTS>
+__global__ void __launch_bounds__(Gemv4Cfg<W, A>::THREADS, 1)
+    gemv4_group64_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
                          const __grid_constant__ CUtensorMap tm_scale, const GemmParams p) {
-  using C = Gemv3Cfg<W, A, QL>;
+  using C = Gemv4Cfg<W, A>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
-  __shared__ __align__(8) uint64_t chain_bar[4][QL];
-  __shared__ float4 acc_smem[4][32];
+  __shared__ __align__(8) uint64_t dot_full[C::DSTAGES][2];
+  __shared__ __align__(8) uint64_t dot_empty[C::DSTAGES][2];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float4* dots_smem = reinterpret_cast<float4*>(smem + C::STAGES * C::STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp == 0 && lane < 3) prefetch_tensormap(lane == 0 ? &tm_act : lane == 1 ? &tm_wgt : &tm_scale);
   const int G = p.G, Mb = p.M;  // token boxes are M rows high (M <= 16)
+  const bool hi = Mb > 8;       // tokens 8..15 present
   const int n_stages = (G + C::GPS - 1) / C::GPS;
   const int n_blocks = (p.N + C::ROWS - 1) / C::ROWS;
-  const int my_blocks = blockIdx.x < n_blocks ? (n_blocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int my_blocks = (int)blockIdx.x < n_blocks ? (n_blocks - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int total = my_blocks * n_stages;
-  const uint32_t stage_tx = C::W_BYTES + Mb * (C::A_BLK * 128 + (DOTS ? 0 : C::GPS * 4));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], C::WARPS);
+      mbar_init(&empty_bar[s], C::DOT_WARPS + C::CHAIN_WARPS);
     }
-    for (int r = 0; r < 4; ++r)
-      for (int q = 0; q < QL; ++q) mbar_init(&chain_bar[r][q], 1);
+    for (int d = 0; d < C::DSTAGES; ++d)
+      for (int r = 0; r < 2; ++r) {
+        mbar_init(&dot_full[d][r], C::QL);
+        mbar_init(&dot_empty[d][r], 2);
+      }
     fence_barrier_init();
   }
   __syncthreads();
 
-  // Lanes 0 (weights), 1 (tokens) and 2 (scales) of the calling warp load stage
-  // `it` into its slot.
-  auto issue = [&](int it) {
-    const int s = it % C::STAGES;
-    const int rb = blockIdx.x + (it / n_stages) * gridDim.x, st = it % n_stages;
-    if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], stage_tx);
-    __syncwarp(0x7u);
-    uint8_t* base = smem + s * C::STAGE_BYTES;
-    if (lane == 0) tma_load_3d(base, &tm_wgt, 0, rb * C::ROWS, st * C::W_BLK, &full_bar[s]);
-    else if (lane == 1) tma_load_3d(base + C::W_BYTES, &tm_act, 0, 0, st * C::A_BLK, &full_bar[s]);
-    else if (!DOTS) tma_load_2d(base + C::W_BYTES + C::A_BYTES, &tm_scale, st * C::GPS, 0, &full_bar[s]);
-  };
-  if (warp == 0 && lane < 3) {
-    for (int it = 0; it < total && it < C::STAGES; ++it) issue(it);
-  }
-
-  const int r = warp & 3, q = warp >> 2;  // row group, K-lane
-  const int gid = lane >> 2, t = lane & 3;
-  const float shift_scale = 1.0f / float(1 << C::SHIFT);
-  const bool tok0 = gid < Mb, tok1 = gid + 8 < Mb, hi = Mb > 8;
-  uint32_t ow[C::GPQ], oa_lo[C::GPQ], oa_hi[C::GPQ];
-#pragma unroll
-  for (int j = 0; j < C::GPQ; ++j) {
-    ow[j] = swizzled_offset<W>(q * C::GPQ + j, t, r * 8 + gid, C::ROWS);
-    oa_lo[j] = swizzled_offset<A>(q * C::GPQ + j, t, gid, Mb);
-    oa_hi[j] = swizzled_offset<A>(q * C::GPQ + j, t, gid + 8, Mb);
-  }
-
-  bool ok = true;
-  // Dots of one stage for this warp's groups, exact fp32 (or the dots export), and
-  // the matching activation scales times 2^-SHIFT (0 for absent tokens and groups).
-  auto compute = [&](int it, float (&dots)[C::GPQ][4], float (&sc)[C::GPQ][2]) {
-    const int s = it % C::STAGES;
-    const int rb = blockIdx.x + (it / n_stages) * gridDim.x, st = it % n_stages;
-    if (!mbar_wait(&full_bar[s], (it / C::STAGES) & 1, kGv3SiteFull)) {
-      ok = false;
-      return;
+  if (warp == C::PRODUCER) {
+    // ------------------------------------------------------------ producer
+    // Lanes 0 (weights), 1 (tokens) and 2 (scales) issue a stage's three boxes in
+    // one instruction.
+    if (lane < 3) {
+      prefetch_tensormap(lane == 0 ? &tm_wgt : lane == 1 ? &tm_act : &tm_scale);
+      const uint32_t stage_tx = C::W_BYTES + Mb * (C::A_BLK * 128 + (DOTS ? 0 : C::GPS * 4));
+      int issued = 0;
+      for (int it = 0; it < total; ++it) {
+        const int s = it % C::STAGES;
+        bool ok = true;
+        if (lane == 0) {
+          if (it >= C::STAGES) ok = mbar_wait(&empty_bar[s], ((it / C::STAGES) & 1) ^ 1, kGv4SiteEmpty);
+          if (ok) mbar_arrive_expect_tx(&full_bar[s], stage_tx);
+        }
+        if (!__shfl_sync(0x7u, ok, 0)) break;
+        const int rb = (int)blockIdx.x + (it / n_stages) * (int)gridDim.x, st = it % n_stages;
+        uint8_t* base = smem + s * C::STAGE_BYTES;
+        if (lane == 0) tma_load_3d(base, &tm_wgt, 0, rb * C::ROWS, st * C::W_BLK, &full_bar[s]);
+        else if (lane == 1) tma_load_3d(base + C::W_BYTES, &tm_act, 0, 0, st * C::A_BLK, &full_bar[s]);
+        else if (!DOTS) tma_load_2d(base + C::W_BYTES + C::A_BYTES, &tm_scale, st * C::GPS, 0, &full_bar[s]);
+        ++issued;
+      }
+      // Never leave the CTA with bulk copies still landing in shared memory.
+      if (lane == 0) {
+        for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it)
+          mbar_wait(&full_bar[it % C::STAGES], (it / C::STAGES) & 1, kGv4SiteDrain);
+      }
     }
-    const uint8_t* w_tile = smem + s * C::STAGE_BYTES;
-    const uint8_t* a_tile = w_tile + C::W_BYTES;
-    if constexpr (!DOTS) {
-      const float* sc_tile = reinterpret_cast<const float*>(a_tile + C::A_BYTES);
+  } else if (warp < C::DOT_WARPS) {
+    // ------------------------------------------------------------ dots
+    const int r = warp & 1, q = warp >> 1;  // 16-row group, K-lane
+    const int gid = lane >> 2, t = lane & 3;
+    uint32_t ow0[C::GPQ], ow1[C::GPQ], oa_lo[C::GPQ], oa_hi[C::GPQ];
+#pragma unroll
+    for (int j = 0; j < C::GPQ; ++j) {
+      ow0[j] = swizzled_offset<W>(q * C::GPQ + j, t, r * 16 + gid, C::ROWS);
+      ow1[j] = swizzled_offset<W>(q * C::GPQ + j, t, r * 16 + 8 + gid, C::ROWS);
+      oa_lo[j] = swizzled_offset<A>(q * C::GPQ + j, t, gid, Mb);
+      oa_hi[j] = swizzled_offset<A>(q * C::GPQ + j, t, gid + 8, Mb);
+    }
+    for (int it = 0; it < total; ++it) {
+      const int s = it % C::STAGES, d = it % C::DSTAGES;
+      if (!mbar_wait(&full_bar[s], (it / C::STAGES) & 1, kGv4SiteFull)) break;
+      if constexpr (!DOTS) {
+        if (it >= C::DSTAGES && !mbar_wait(&dot_empty[d][r], ((it / C::DSTAGES) & 1) ^ 1, kGv4SiteDotEmpty)) break;
+      }
+      const int rb = (int)blockIdx.x + (it / n_stages) * (int)gridDim.x, st = it % n_stages;
+      const uint8_t* w_tile = smem + s * C::STAGE_BYTES;
+      const uint8_t* a_tile = w_tile + C::W_BYTES;
 #pragma unroll
       for (int j = 0; j < C::GPQ; ++j) {
-        sc[j][0] = tok0 ? sc_tile[gid * C::GPS + q * C::GPQ + j] * shift_scale : 0.f;
-        sc[j][1] = tok1 ? sc_tile[(gid + 8) * C::GPS + q * C::GPQ + j] * shift_scale : 0.f;
-      }
-    }
+        const uint4 a_lo = load_codes16_at<A>(a_tile + oa_lo[j]);
+        const uint4 a_hi = hi ? load_codes16_at<A>(a_tile + oa_hi[j]) : make_uint4(0, 0, 0, 0);
+        const uint32_t a0[4] = {a_lo.x, a_hi.x, a_lo.y, a_hi.y};
+        const uint32_t a1[4] = {a_lo.z, a_hi.z, a_lo.w, a_hi.w};
 #pragma unroll
-    for (int j = 0; j < C::GPQ; ++j) {
-      const uint4 wq = load_codes16_at<W>(w_tile + ow[j]);
-      const uint4 a_lo = load_codes16_at<A>(a_tile + oa_lo[j]);
-      const uint4 a_hi = hi ? load_codes16_at<A>(a_tile + oa_hi[j]) : make_uint4(0, 0, 0, 0);
-      int32_t d[4] = {0, 0, 0, 0};
-      const uint32_t a0[4] = {a_lo.x, a_hi.x, a_lo.y, a_hi.y};
-      mma_s8_16832(d, a0, wq.x, wq.y);
-      const uint32_t a1[4] = {a_lo.z, a_hi.z, a_lo.w, a_hi.w};
-      mma_s8_16832(d, a1, wq.z, wq.w);
-      if constexpr (DOTS) {
-        const int g = st * C::GPS + q * C::GPQ + j;
+        for (int b = 0; b < 2; ++b) {
+          const uint4 wq = load_codes16_at<W>(w_tile + (b ? ow1[j] : ow0[j]));
+          int32_t dd[4] = {0, 0, 0, 0};
+          mma_s8_16832(dd, a0, wq.x, wq.y);
+          mma_s8_16832(dd, a1, wq.z, wq.w);
+          const int blk8 = r * 2 + b;  // 8-row block of the 32-row tile
+          if constexpr (DOTS) {
+            const int g = st * C::GPS + q * C::GPQ + j;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int m = (i >> 1) * 8 + gid;
-          const int n = rb * C::ROWS + r * 8 + 2 * t + (i & 1);
-          if (m < p.M && n < p.N && g < G) p.dots[((int64_t)m * p.N + n) * G + g] = d[i] >> C::SHIFT;
+            for (int i = 0; i < 4; ++i) {
+              const int m = (i >> 1) * 8 + gid;
+              const int n = rb * C::ROWS + blk8 * 8 + 2 * t + (i & 1);
+              if (m < p.M && n < p.N && g < G) p.dots[((int64_t)m * p.N + n) * G + g] = dd[i] >> C::SHIFT;
+            }
+          } else {
+            float4* dst = dots_smem + ((d * 4 + blk8) * C::GPS + q * C::GPQ + j) * 32 + lane;
+            if (hi) *dst = make_float4(exact_float(dd[0]), exact_float(dd[1]), exact_float(dd[2]), exact_float(dd[3]));
+            else *reinterpret_cast<float2*>(dst) = make_float2(exact_float(dd[0]), exact_float(dd[1]));
+          }
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dots[j][i] = exact_float(d[i]);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (!DOTS) mbar_arrive(&dot_full[d][r]);
+        mbar_arrive(&empty_bar[s]);
       }
     }
-    // Release the slot; the round-robin refiller waits for all warps, then loads
-    // stage it + STAGES into it.
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[s]);
-    if (warp == it % C::WARPS && it + C::STAGES < total && lane < 3) {
-      bool w_ok = true;
-      if (lane == 0) w_ok = mbar_wait(&empty_bar[s], (it / C::STAGES) & 1, kGv3SiteEmpty);
-      if (__shfl_sync(0x7u, w_ok, 0)) issue(it + C::STAGES);
-      else ok = false;
-    }
-  };
-  // Weight scales and bias of the last K-lane's output rows, loaded when a block
-  // starts so that the block's last step issues no dependent global load.
-  const bool has_bias = p.bias_dtype != kDtNone;
-  float ws_pre[2] = {0.f, 0.f}, bias_pre[2] = {0.f, 0.f};
-  // Fold one stage's dots into the chain (K order: K-lane 0 .. QL-1, then the next stage).
-  auto chain = [&](int it, const float (&dots)[C::GPQ][4], const float (&sc)[C::GPQ][2]) {
-    const int rb = blockIdx.x + (it / n_stages) * gridDim.x, st = it % n_stages;
-    const bool last = q == QL - 1 && st == n_stages - 1;
-    if (q == QL - 1 && st == 0) {
-#pragma unroll
-      for (int i2 = 0; i2 < 2; ++i2) {
-        const int n = rb * C::ROWS + r * 8 + 2 * t + i2;
-        ws_pre[i2] = n < p.N ? __ldg(p.w_scale + n) : 0.f;
-        bias_pre[i2] = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
-      }
-    }
+  } else {
+    // ------------------------------------------------------------ chain
+    const int blk8 = warp - C::DOT_WARPS, r = blk8 >> 1;  // 8-row block, its 16-row group
+    const int gid = lane >> 2, t = lane & 3;
+    const bool tok0 = gid < Mb, tok1 = gid + 8 < Mb;
+    const bool has_bias = p.bias_dtype != kDtNone;
+    const float shift_scale = 1.0f / float(1 << C::SHIFT);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    // Every hand-off except the CTA's very first waits for its predecessor, also
-    // at a block's first stage (where it starts from zero), so that the shared
-    // accumulator slot has been read before it is overwritten.
-    if (q > 0 || it > 0) {
-      const int qp = (q + QL - 1) % QL;
-      const int prev = q > 0 ? it : it - 1;
-      if (!mbar_wait(&chain_bar[r][qp], prev & 1, kGv3SiteChain)) {
-        ok = false;
-        return;
-      }
-      if (q > 0 || st > 0) acc = acc_smem[r][lane];
-    }
-    // A block's last step only reads the slot: free it for the next block at once.
-    if (last) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&chain_bar[r][q]);
-    }
-    // Groups past the end of K have dot 0 and scale 0: acc += 0 * 0 keeps acc.
+    float ws_pre[2] = {0.f, 0.f}, bias_pre[2] = {0.f, 0.f};
+    for (int it = 0; it < total; ++it) {
+      const int s = it % C::STAGES, d = it % C::DSTAGES;
+      const int rb = (int)blockIdx.x + (it / n_stages) * (int)gridDim.x, st = it % n_stages;
+      if constexpr (DOTS) {
+        if (!mbar_wait(&full_bar[s], (it / C::STAGES) & 1, kGv4SiteFull)) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[s]);
+        continue;
+      } else {
+        if (st == 0) {
+          // Weight scales and bias of this row block, loaded early.
 #pragma unroll
-    for (int j = 0; j < C::GPQ; ++j) {
-      acc.x = fmaf(dots[j][0], sc[j][0], acc.x);
-      acc.y = fmaf(dots[j][1], sc[j][0], acc.y);
-      acc.z = fmaf(dots[j][2], sc[j][1], acc.z);
-      acc.w = fmaf(dots[j][3], sc[j][1], acc.w);
-    }
-    if (last) {
+          for (int i2 = 0; i2 < 2; ++i2) {
+            const int n = rb * C::ROWS + blk8 * 8 + 2 * t + i2;
+            ws_pre[i2] = n < p.N ? __ldg(p.w_scale + n) : 0.f;
+            bias_pre[i2] = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+          }
+          acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (!mbar_wait(&full_bar[s], (it / C::STAGES) & 1, kGv4SiteFull)) break;
+        if (!mbar_wait(&dot_full[d][r], (it / C::DSTAGES) & 1, kGv4SiteDotFull)) break;
+        const float* sc_tile = reinterpret_cast<const float*>(smem + s * C::STAGE_BYTES + C::W_BYTES + C::A_BYTES);
+        const float4* dslot = dots_smem + ((d * 4 + blk8) * C::GPS) * 32 + lane;
+        // Groups past the end of K have dot 0 and scale 0 (zero fill): acc += 0 * 0.
+        if (hi) {
 #pragma unroll
-      for (int i2 = 0; i2 < 2; ++i2) {
-        const int n = rb * C::ROWS + r * 8 + 2 * t + i2;
-        if (n >= p.N) continue;
-        const float ws = ws_pre[i2], bias = bias_pre[i2];
-        const float a0v = i2 ? acc.y : acc.x, a1v = i2 ? acc.w : acc.z;
-        if (tok0) store_scalar(p, (int64_t)gid * p.N + n, has_bias ? fmaf(a0v, ws, bias) : a0v * ws);
-        if (tok1) store_scalar(p, (int64_t)(gid + 8) * p.N + n, has_bias ? fmaf(a1v, ws, bias) : a1v * ws);
+          for (int g = 0; g < C::GPS; ++g) {
+            const float4 dv = dslot[g * 32];
+            const float s0 = tok0 ? sc_tile[gid * C::GPS + g] * shift_scale : 0.f;
+            const float s1 = tok1 ? sc_tile[(gid + 8) * C::GPS + g] * shift_scale : 0.f;
+            acc.x = fmaf(dv.x, s0, acc.x);
+            acc.y = fmaf(dv.y, s0, acc.y);
+            acc.z = fmaf(dv.z, s1, acc.z);
+            acc.w = fmaf(dv.w, s1, acc.w);
+          }
+        } else {
+#pragma unroll
+          for (int g = 0; g < C::GPS; ++g) {
+            const float2 dv = *reinterpret_cast<const float2*>(dslot + g * 32);
+            const float s0 = tok0 ? sc_tile[gid * C::GPS + g] * shift_scale : 0.f;
+            acc.x = fmaf(dv.x, s0, acc.x);
+            acc.y = fmaf(dv.y, s0, acc.y);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&dot_empty[d][r]);
+          mbar_arrive(&empty_bar[s]);
+        }
+        if (st == n_stages - 1) {
+#pragma unroll
+          for (int i2 = 0; i2 < 2; ++i2) {
+            const int n = rb * C::ROWS + blk8 * 8 + 2 * t + i2;
+            if (n >= p.N) continue;
+            const float ws = ws_pre[i2], bias = bias_pre[i2];
+            const float a0v = i2 ? acc.y : acc.x, a1v = i2 ? acc.w : acc.z;
+            if (tok0) store_scalar(p, (int64_t)gid * p.N + n, has_bias ? fmaf(a0v, ws, bias) : a0v * ws);
+            if (tok1) store_scalar(p, (int64_t)(gid + 8) * p.N + n, has_bias ? fmaf(a1v, ws, bias) : a1v * ws);
+          }
+        }
       }
-    } else {
-      acc_smem[r][lane] = acc;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&chain_bar[r][q]);
     }
-  };
-
-  float dots_a[C::GPQ][4], sc_a[C::GPQ][2], dots_b[C::GPQ][4], sc_b[C::GPQ][2];
-  if (total > 0) compute(0, dots_a, sc_a);
-  for (int it = 0; it < total && ok; it += 2) {
-    // Ping-pong register sets (constant indices keep them in registers).
-    if (it + 1 < total) compute(it + 1, dots_b, sc_b);
-    if (!ok) break;
-    if constexpr (!DOTS) chain(it, dots_a, sc_a);
-    if (!ok || it + 1 >= total) break;
-    if (it + 2 < total) compute(it + 2, dots_a, sc_a);
-    if (!ok) break;
-    if constexpr (!DOTS) chain(it + 1, dots_b, sc_b);
-  }
-  // Never leave the CTA with bulk copies still landing in shared memory.
-  if (warp == 0 && lane == 0) {
-    for (int it = total > C::STAGES ? total - C::STAGES : 0; it < total; ++it)
-      mbar_wait(&full_bar[it % C::STAGES], (it / C::STAGES) & 1, kGv3SiteDrain);
   }
 }
 
-template <int W, int A, int QL>
-static cudaError_t launch_gemv3_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
+template <int W, int A>
+static cudaError_t launch_gemv4_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
                                   const GemmParams& p, int num_sms, cudaStream_t stream) {
-  using C = Gemv3Cfg<W, A, QL>;
+  using C = Gemv4Cfg<W, A>;
   const bool dots = p.dots != nullptr;
-  auto kernel = dots ? gemv3_group64_kernel<W, A, QL, true> : gemv3_group64_kernel<W, A, QL, false>;
+  auto kernel = dots ? gemv4_group64_kernel<W, A, true> : gemv4_group64_kernel<W, A, false>;
   int dev = 0;
   cudaGetDevice(&dev);
   static bool configured[2][64] = {};
@@ -569,12 +567,10 @@ static cudaError_t launch_gemv_t(const CUtensorMap& ta, const CUtensorMap& tw, c
 
 cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap* ts,
                                 const GemmParams& p, int num_sms, cudaStream_t stream) {
-  const int ql = gemv_klanes();
 #define ACTUNE_CASE(WW, AA)                                                                                  \
   if (W == WW && A == AA) {                                                                                  \
     if (ts != nullptr)                                                                                       \
-      return ql == 2 ? launch_gemv3_t<WW, AA, 2>(ta, tw, *ts, p, num_sms, stream)                            \
-                     : launch_gemv3_t<WW, AA, 4>(ta, tw, *ts, p, num_sms, stream);                           \
+      return launch_gemv4_t<WW, AA>(ta, tw, *ts, p, num_sms, stream);                                        \
     return p.M <= 16 ? launch_gemv_t<WW, AA, 1>(ta, tw, p, stream) : launch_gemv_t<WW, AA, 2>(ta, tw, p, stream); \
   }
   ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
