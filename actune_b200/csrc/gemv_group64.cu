@@ -22,6 +22,8 @@
 // 16t..16t+15), which leaves every dot unchanged.  Sub-byte codes go to the top bits
 // of int8 (code * 2^(8-bits)); the power of two is removed exactly from the
 // activation scale.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -309,45 +311,50 @@ __device__ __forceinline__ uint32_t swizzled_offset(int gl, int t, int r, int bo
 // is stored and read.  Shared-memory traffic per stage is what bounds this kernel
 // (the copies, the token fragments and the dot round trip share 128 B/clk).
 // A stage slot is free once the 16 dot warps and the 4 chain warps released it.
-template <int W, int A>
+template <int W, int A, bool HI>
 struct Gemv4Cfg {
-  static constexpr int ROWS = 32, TOK = 16, KSTG = 1024, GPS = 16, QL = 8, GPQ = GPS / QL;
+  static constexpr int ROWS = 32, TOK = HI ? 16 : 8, KSTG = 1024, GPS = 16, QL = 8, GPQ = GPS / QL;
   static constexpr int DOT_WARPS = 16, CHAIN_WARPS = 4, PRODUCER = DOT_WARPS + CHAIN_WARPS;
   static constexpr int THREADS = 32 * (PRODUCER + 1);
   static constexpr int A_BLK = KSTG * A / 8 / 128;
   static constexpr int W_BLK = KSTG * W / 8 / 128;
   static constexpr int W_BYTES = W_BLK * ROWS * 128;  // multiple of 4096
-  static constexpr int A_BYTES = A_BLK * TOK * 128;
+  static constexpr int A_BYTES = A_BLK * TOK * 128;   // multiple of 1024
   static constexpr int SC_BYTES = TOK * GPS * 4;
   static constexpr int STAGE_BYTES = (W_BYTES + A_BYTES + SC_BYTES + 1023) / 1024 * 1024;
-  // Dot buffers: [8-row block (4)][group of the stage][lane] float4 (lane's d0..d3).
-  static constexpr int DOT_BYTES = 4 * GPS * 32 * 16;  // 32 KB
+  // Dot buffers: [8-row block (4)][group of the stage][lane] of the lane's d0..d3
+  // (float4), or d0, d1 only (float2) when there are at most 8 tokens; plus a copy
+  // of the stage's activation scales per 16-row group.
+  static constexpr int DOT_LANE_BYTES = HI ? 16 : 8;
+  static constexpr int DOT_BYTES = 4 * GPS * 32 * DOT_LANE_BYTES;
+  static constexpr int DSC_BYTES = 2 * SC_BYTES;
   static constexpr int DSTAGES = 2;
-  static constexpr int RING_BUDGET = 224 * 1024 - DSTAGES * DOT_BYTES;  // 227 KB per CTA at most
+  static constexpr int RING_BUDGET = 224 * 1024 - DSTAGES * (DOT_BYTES + DSC_BYTES);  // 227 KB per CTA at most
   static constexpr int STAGES_FIT = RING_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + DSTAGES * DOT_BYTES + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + DSTAGES * (DOT_BYTES + DSC_BYTES) + 1024;
   static constexpr int SHIFT = (8 - A) + (8 - W);
   static_assert(STAGES >= 2, "ring depth");
 };
 
 enum : int { kGv4SiteFull = 61, kGv4SiteEmpty, kGv4SiteDotFull, kGv4SiteDotEmpty, kGv4SiteDrain };
 
-template <int W, int A, bool DOTS>
-__global__ void __launch_bounds__(Gemv4Cfg<W, A>::THREADS, 1)
+template <int W, int A, bool HI, bool DOTS>
+__global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
     gemv4_group64_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
                          const __grid_constant__ CUtensorMap tm_scale, const GemmParams p) {
-  using C = Gemv4Cfg<W, A>;
+  using C = Gemv4Cfg<W, A, HI>;
+  using DotT = typename std::conditional<HI, float4, float2>::type;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
   __shared__ __align__(8) uint64_t dot_full[C::DSTAGES][2];
   __shared__ __align__(8) uint64_t dot_empty[C::DSTAGES][2];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float4* dots_smem = reinterpret_cast<float4*>(smem + C::STAGES * C::STAGE_BYTES);
+  DotT* dots_smem = reinterpret_cast<DotT*>(smem + C::STAGES * C::STAGE_BYTES);
+  float* dsc_smem = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + C::DSTAGES * C::DOT_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = p.G, Mb = p.M;  // token boxes are M rows high (M <= 16)
-  const bool hi = Mb > 8;       // tokens 8..15 present
+  const int G = p.G, Mb = p.M;  // token boxes are M rows high (M <= TOK)
   const int n_stages = (G + C::GPS - 1) / C::GPS;
   const int n_blocks = (p.N + C::ROWS - 1) / C::ROWS;
   const int my_blocks = (int)blockIdx.x < n_blocks ? (n_blocks - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
@@ -356,7 +363,7 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], C::DOT_WARPS + C::CHAIN_WARPS);
+      mbar_init(&empty_bar[s], C::DOT_WARPS);
     }
     for (int d = 0; d < C::DSTAGES; ++d)
       for (int r = 0; r < 2; ++r) {
@@ -417,10 +424,20 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A>::THREADS, 1)
       const int rb = (int)blockIdx.x + (it / n_stages) * (int)gridDim.x, st = it % n_stages;
       const uint8_t* w_tile = smem + s * C::STAGE_BYTES;
       const uint8_t* a_tile = w_tile + C::W_BYTES;
+      if constexpr (!DOTS) {
+        // K-lane 0 copies the stage's scales for its row group's chain warps, so that
+        // the stage slot is free once the dots are written.
+        if (q == 0) {
+          const float4* src = reinterpret_cast<const float4*>(a_tile + C::A_BYTES);
+          float4* dst = reinterpret_cast<float4*>(dsc_smem + (d * 2 + r) * (C::TOK * C::GPS));
+          for (int i = lane; i < Mb * C::GPS / 4; i += 32) dst[i] = src[i];
+        }
+      }
 #pragma unroll
       for (int j = 0; j < C::GPQ; ++j) {
         const uint4 a_lo = load_codes16_at<A>(a_tile + oa_lo[j]);
-        const uint4 a_hi = hi ? load_codes16_at<A>(a_tile + oa_hi[j]) : make_uint4(0, 0, 0, 0);
+        uint4 a_hi = make_uint4(0, 0, 0, 0);
+        if constexpr (HI) a_hi = load_codes16_at<A>(a_tile + oa_hi[j]);
         const uint32_t a0[4] = {a_lo.x, a_hi.x, a_lo.y, a_hi.y};
         const uint32_t a1[4] = {a_lo.z, a_hi.z, a_lo.w, a_hi.w};
 #pragma unroll
@@ -439,9 +456,11 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A>::THREADS, 1)
               if (m < p.M && n < p.N && g < G) p.dots[((int64_t)m * p.N + n) * G + g] = dd[i] >> C::SHIFT;
             }
           } else {
-            float4* dst = dots_smem + ((d * 4 + blk8) * C::GPS + q * C::GPQ + j) * 32 + lane;
-            if (hi) *dst = make_float4(exact_float(dd[0]), exact_float(dd[1]), exact_float(dd[2]), exact_float(dd[3]));
-            else *reinterpret_cast<float2*>(dst) = make_float2(exact_float(dd[0]), exact_float(dd[1]));
+            DotT* dst = dots_smem + ((d * 4 + blk8) * C::GPS + q * C::GPQ + j) * 32 + lane;
+            if constexpr (HI)
+              *dst = make_float4(exact_float(dd[0]), exact_float(dd[1]), exact_float(dd[2]), exact_float(dd[3]));
+            else
+              *dst = make_float2(exact_float(dd[0]), exact_float(dd[1]));
           }
         }
       }
@@ -451,86 +470,67 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A>::THREADS, 1)
         mbar_arrive(&empty_bar[s]);
       }
     }
-  } else {
+  } else if constexpr (!DOTS) {
     // ------------------------------------------------------------ chain
     const int blk8 = warp - C::DOT_WARPS, r = blk8 >> 1;  // 8-row block, its 16-row group
     const int gid = lane >> 2, t = lane & 3;
-    const bool tok0 = gid < Mb, tok1 = gid + 8 < Mb;
+    const bool tok0 = gid < Mb, tok1 = HI && gid + 8 < Mb;
     const bool has_bias = p.bias_dtype != kDtNone;
     const float shift_scale = 1.0f / float(1 << C::SHIFT);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float ws_pre[2] = {0.f, 0.f}, bias_pre[2] = {0.f, 0.f};
     for (int it = 0; it < total; ++it) {
-      const int s = it % C::STAGES, d = it % C::DSTAGES;
+      const int d = it % C::DSTAGES;
       const int rb = (int)blockIdx.x + (it / n_stages) * (int)gridDim.x, st = it % n_stages;
-      if constexpr (DOTS) {
-        if (!mbar_wait(&full_bar[s], (it / C::STAGES) & 1, kGv4SiteFull)) break;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[s]);
-        continue;
-      } else {
-        if (st == 0) {
-          // Weight scales and bias of this row block, loaded early.
+      if (st == 0) {
+        // Weight scales and bias of this row block, loaded early.
 #pragma unroll
-          for (int i2 = 0; i2 < 2; ++i2) {
-            const int n = rb * C::ROWS + blk8 * 8 + 2 * t + i2;
-            ws_pre[i2] = n < p.N ? __ldg(p.w_scale + n) : 0.f;
-            bias_pre[i2] = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
-          }
-          acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i2 = 0; i2 < 2; ++i2) {
+          const int n = rb * C::ROWS + blk8 * 8 + 2 * t + i2;
+          ws_pre[i2] = n < p.N ? __ldg(p.w_scale + n) : 0.f;
+          bias_pre[i2] = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
         }
-        if (!mbar_wait(&full_bar[s], (it / C::STAGES) & 1, kGv4SiteFull)) break;
-        if (!mbar_wait(&dot_full[d][r], (it / C::DSTAGES) & 1, kGv4SiteDotFull)) break;
-        const float* sc_tile = reinterpret_cast<const float*>(smem + s * C::STAGE_BYTES + C::W_BYTES + C::A_BYTES);
-        const float4* dslot = dots_smem + ((d * 4 + blk8) * C::GPS) * 32 + lane;
-        // Groups past the end of K have dot 0 and scale 0 (zero fill): acc += 0 * 0.
-        if (hi) {
+        acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      if (!mbar_wait(&dot_full[d][r], (it / C::DSTAGES) & 1, kGv4SiteDotFull)) break;
+      const float* sc = dsc_smem + (d * 2 + r) * (C::TOK * C::GPS);
+      const DotT* dslot = dots_smem + ((d * 4 + blk8) * C::GPS) * 32 + lane;
+      // Groups past the end of K have dot 0 and scale 0 (zero fill): acc += 0 * 0.
 #pragma unroll
-          for (int g = 0; g < C::GPS; ++g) {
-            const float4 dv = dslot[g * 32];
-            const float s0 = tok0 ? sc_tile[gid * C::GPS + g] * shift_scale : 0.f;
-            const float s1 = tok1 ? sc_tile[(gid + 8) * C::GPS + g] * shift_scale : 0.f;
-            acc.x = fmaf(dv.x, s0, acc.x);
-            acc.y = fmaf(dv.y, s0, acc.y);
-            acc.z = fmaf(dv.z, s1, acc.z);
-            acc.w = fmaf(dv.w, s1, acc.w);
-          }
-        } else {
-#pragma unroll
-          for (int g = 0; g < C::GPS; ++g) {
-            const float2 dv = *reinterpret_cast<const float2*>(dslot + g * 32);
-            const float s0 = tok0 ? sc_tile[gid * C::GPS + g] * shift_scale : 0.f;
-            acc.x = fmaf(dv.x, s0, acc.x);
-            acc.y = fmaf(dv.y, s0, acc.y);
-          }
+      for (int g = 0; g < C::GPS; ++g) {
+        const DotT dv = dslot[g * 32];
+        const float s0 = tok0 ? sc[gid * C::GPS + g] * shift_scale : 0.f;
+        acc.x = fmaf(dv.x, s0, acc.x);
+        acc.y = fmaf(dv.y, s0, acc.y);
+        if constexpr (HI) {
+          const float s1 = tok1 ? sc[(gid + 8) * C::GPS + g] * shift_scale : 0.f;
+          acc.z = fmaf(dv.z, s1, acc.z);
+          acc.w = fmaf(dv.w, s1, acc.w);
         }
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&dot_empty[d][r]);
-          mbar_arrive(&empty_bar[s]);
-        }
-        if (st == n_stages - 1) {
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dot_empty[d][r]);
+      if (st == n_stages - 1) {
 #pragma unroll
-          for (int i2 = 0; i2 < 2; ++i2) {
-            const int n = rb * C::ROWS + blk8 * 8 + 2 * t + i2;
-            if (n >= p.N) continue;
-            const float ws = ws_pre[i2], bias = bias_pre[i2];
-            const float a0v = i2 ? acc.y : acc.x, a1v = i2 ? acc.w : acc.z;
-            if (tok0) store_scalar(p, (int64_t)gid * p.N + n, has_bias ? fmaf(a0v, ws, bias) : a0v * ws);
-            if (tok1) store_scalar(p, (int64_t)(gid + 8) * p.N + n, has_bias ? fmaf(a1v, ws, bias) : a1v * ws);
-          }
+        for (int i2 = 0; i2 < 2; ++i2) {
+          const int n = rb * C::ROWS + blk8 * 8 + 2 * t + i2;
+          if (n >= p.N) continue;
+          const float ws = ws_pre[i2], bias = bias_pre[i2];
+          const float a0v = i2 ? acc.y : acc.x, a1v = i2 ? acc.w : acc.z;
+          if (tok0) store_scalar(p, (int64_t)gid * p.N + n, has_bias ? fmaf(a0v, ws, bias) : a0v * ws);
+          if (tok1) store_scalar(p, (int64_t)(gid + 8) * p.N + n, has_bias ? fmaf(a1v, ws, bias) : a1v * ws);
         }
       }
     }
   }
 }
 
-template <int W, int A>
-static cudaError_t launch_gemv4_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
-                                  const GemmParams& p, int num_sms, cudaStream_t stream) {
-  using C = Gemv4Cfg<W, A>;
+template <int W, int A, bool HI>
+static cudaError_t launch_gemv4_hi(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
+                                   const GemmParams& p, int num_sms, cudaStream_t stream) {
+  using C = Gemv4Cfg<W, A, HI>;
   const bool dots = p.dots != nullptr;
-  auto kernel = dots ? gemv4_group64_kernel<W, A, true> : gemv4_group64_kernel<W, A, false>;
+  auto kernel = dots ? gemv4_group64_kernel<W, A, HI, true> : gemv4_group64_kernel<W, A, HI, false>;
   int dev = 0;
   cudaGetDevice(&dev);
   static bool configured[2][64] = {};
@@ -544,6 +544,13 @@ static cudaError_t launch_gemv4_t(const CUtensorMap& ta, const CUtensorMap& tw, 
   const int grid = blocks < num_sms ? blocks : num_sms;
   kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, ts, p);
   return cudaGetLastError();
+}
+
+template <int W, int A>
+static cudaError_t launch_gemv4_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
+                                  const GemmParams& p, int num_sms, cudaStream_t stream) {
+  return p.M > 8 ? launch_gemv4_hi<W, A, true>(ta, tw, ts, p, num_sms, stream)
+                 : launch_gemv4_hi<W, A, false>(ta, tw, ts, p, num_sms, stream);
 }
 
 template <int W, int A, int MT>
