@@ -293,6 +293,49 @@ __device__ __forceinline__ uint2 unpack_w4_word(uint32_t x) {
   return make_uint2(__byte_perm(lo, hi, 0x5140), __byte_perm(lo, hi, 0x7362));
 }
 
+// Group-64 activation quantization of one lane's 8 consecutive values, the group
+// spread over 8 consecutive lanes of the warp (lanes 8s .. 8s+7, in K order; all 32
+// lanes must call it together).  Restates actune/kernels/grouped.py:55-71:
+//   scale = max(absmax, 1e-8) / (2^(A-1) - 1)               IEEE division
+//   code  = clamp(rint(x / scale), -2^(A-1), 2^(A-1) - 1)    IEEE division, RNE
+// and packs the lane's 8 codes little-endian, code i at bit i*A of `word`.
+// Returns the group's scale (the same in all 8 lanes).
+template <int A>
+__device__ __forceinline__ float quantize_lane8(const float (&v)[8], uint32_t (&word)[2]) {
+  constexpr float kPositive = float((1 << (A - 1)) - 1);
+  constexpr float kLo = -float(1 << (A - 1));
+  constexpr int kMask = (1 << A) - 1;
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+  const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), kPositive);
+  word[0] = word[1] = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float q = rintf(__fdiv_rn(v[i], scale));
+    q = fminf(fmaxf(q, kLo), kPositive);
+    const uint32_t field = (uint32_t)((int)q) & kMask;
+    const int bit = i * A;
+    word[bit >> 5] |= field << (bit & 31);
+  }
+  return scale;
+}
+
+// Stores a lane's packed codes (8*A bits) at dst.
+template <int A>
+__device__ __forceinline__ void store_lane_codes(uint8_t* dst, const uint32_t (&word)[2]) {
+  if constexpr (A == 8) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(word[0], word[1]);
+  } else if constexpr (A == 4) {
+    *reinterpret_cast<uint32_t*>(dst) = word[0];
+  } else {
+    *reinterpret_cast<uint16_t*>(dst) = (uint16_t)word[0];
+  }
+}
+
 // 4 packed bytes (16 int2 codes, element 4j+i at bits 2i of byte j) -> 16 bytes.
 __device__ __forceinline__ uint4 unpack_w2_word(uint32_t x) {
   const uint32_t t0 = (x << 6) & 0xC0C0C0C0u;

@@ -1,6 +1,8 @@
 // bf16 glue kernels for the Llama/Gemma-shaped benchmark backbones (sm_100a):
 // fused residual-add + RMSNorm, rotary embedding on a fused QKV buffer, and
-// SiLU(gate) * up.  They are not part of the packed-integer path; they keep the
+// SiLU(gate) * up, optionally also quantizing their output to the group-64
+// packed activation format the next projection reads.  They are not part of the
+// packed-integer path; they keep the
 // surrounding model from being launch-bound (one launch each instead of the
 // several elementwise torch kernels the same math would take).
 #include <cuda_bf16.h>
@@ -9,6 +11,7 @@
 
 #include "actune_b200.h"
 #include "actune_b200_harness.h"
+#include "common.cuh"
 
 namespace {
 
@@ -121,13 +124,16 @@ __device__ __forceinline__ float bf16_round(float v) { return bf2f(__float2bfloa
 
 // One CTA (256 threads) per row, CPT chunks of 8 elements per thread kept in
 // registers: D <= 2048 * CPT, D % 8 == 0.  Same arithmetic as rmsnorm_kernel.
-template <int CPT>
+// QA > 0: the bf16 output is also quantized (group 64, QA bits) into qpacked /
+// qscales, from the rounded values it stores (D % 256 == 0: whole warps per row).
+template <int CPT, int QA>
 __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const __nv_bfloat16* __restrict__ x,
                                                           const __nv_bfloat16* __restrict__ residual,
                                                           const __nv_bfloat16* __restrict__ weight,
                                                           __nv_bfloat16* __restrict__ out,
                                                           __nv_bfloat16* __restrict__ residual_out, int D, float eps,
-                                                          int gemma) {
+                                                          int gemma, uint8_t* __restrict__ qpacked,
+                                                          float* __restrict__ qscales) {
   __shared__ float red[8];
   const int64_t base = (int64_t)blockIdx.x * D;
   float v[CPT][8];
@@ -168,7 +174,16 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const __nv_bfloat16* _
       unpack8(__ldg(reinterpret_cast<const uint4*>(weight + i)), w);
 #pragma unroll
       for (int k = 0; k < 8; ++k) o[k] = gemma ? v[c][k] * inv * (1.f + w[k]) : w[k] * bf16_round(v[c][k] * inv);
-      *reinterpret_cast<uint4*>(out + base + i) = pack8(o);
+      const uint4 stored = pack8(o);
+      *reinterpret_cast<uint4*>(out + base + i) = stored;
+      if constexpr (QA > 0) {
+        float q[8];
+        unpack8(stored, q);
+        uint32_t word[2];
+        const float scale = actune::quantize_lane8<QA>(q, word);
+        actune::store_lane_codes<QA>(qpacked + (base + i) * QA / 8, word);
+        if ((threadIdx.x & 7) == 0) qscales[(base + i) / 64] = scale;
+      }
     }
   }
 }
@@ -203,29 +218,53 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(__nv_bfloat16* __restrict
   }
 }
 
-// Gated activation, 8 outputs per thread (I % 8 == 0).
+// Gated activation, 8 outputs per thread (I % 8 == 0).  QA > 0: the output is also
+// quantized (group 64, QA bits; I % 64 == 0) from the rounded values it stores.
+// Warps step through the items together so that each 64-group's 8 lanes shuffle
+// as one segment.
+template <int QA>
 __global__ void __launch_bounds__(256) gated_act_vec_kernel(const __nv_bfloat16* __restrict__ gu,
-                                                            __nv_bfloat16* __restrict__ out, int T, int I, int gelu) {
+                                                            __nv_bfloat16* __restrict__ out, int T, int I, int gelu,
+                                                            uint8_t* __restrict__ qpacked,
+                                                            float* __restrict__ qscales) {
   const int per_row = I / 8;
   const int64_t total = (int64_t)T * per_row;
-  for (int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; item < total;
-       item += (int64_t)gridDim.x * blockDim.x) {
-    const int t = (int)(item / per_row), c = (int)(item % per_row) * 8;
-    float g[8], u[8], o[8];
-    unpack8(__ldg(reinterpret_cast<const uint4*>(gu + (int64_t)t * 2 * I + c)), g);
-    unpack8(__ldg(reinterpret_cast<const uint4*>(gu + (int64_t)t * 2 * I + I + c)), u);
+  const int lane = threadIdx.x & 31;
+  for (int64_t wbase = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); wbase < total;
+       wbase += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t item = wbase + lane;
+    const bool live = item < total;
+    uint4 stored = make_uint4(0, 0, 0, 0);
+    if (live) {
+      const int t = (int)(item / per_row), c = (int)(item % per_row) * 8;
+      float g[8], u[8], o[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(gu + (int64_t)t * 2 * I + c)), g);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(gu + (int64_t)t * 2 * I + I + c)), u);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float a;
-      if (gelu) {
-        const float kk = 0.7978845608028654f;  // sqrt(2/pi)
-        a = 0.5f * g[k] * (1.f + tanhf(kk * (g[k] + 0.044715f * g[k] * g[k] * g[k])));
-      } else {
-        a = g[k] / (1.f + __expf(-g[k]));
+      for (int k = 0; k < 8; ++k) {
+        float a;
+        if (gelu) {
+          const float kk = 0.7978845608028654f;  // sqrt(2/pi)
+          a = 0.5f * g[k] * (1.f + tanhf(kk * (g[k] + 0.044715f * g[k] * g[k] * g[k])));
+        } else {
+          a = g[k] / (1.f + __expf(-g[k]));
+        }
+        o[k] = bf16_round(a) * u[k];
       }
-      o[k] = bf16_round(a) * u[k];
+      stored = pack8(o);
+      *reinterpret_cast<uint4*>(out + item * 8) = stored;
     }
-    *reinterpret_cast<uint4*>(out + item * 8) = pack8(o);
+    if constexpr (QA > 0) {
+      // Groups never straddle live and dead items: total and wbase are multiples of 8.
+      float q[8];
+      unpack8(stored, q);
+      uint32_t word[2];
+      const float scale = actune::quantize_lane8<QA>(q, word);
+      if (live) {
+        actune::store_lane_codes<QA>(qpacked + item * QA, word);
+        if ((lane & 7) == 0) qscales[item / 8] = scale;
+      }
+    }
   }
 }
 
@@ -235,6 +274,16 @@ int grid_for(int64_t n) {
   int64_t b = (n + 255) / 256;
   if (b > 148 * 16) b = 148 * 16;
   return (int)(b < 1 ? 1 : b);
+}
+
+template <int QA>
+cudaError_t launch_rmsnorm_q(const __nv_bfloat16* xb, const __nv_bfloat16* rb, const __nv_bfloat16* wb,
+                             __nv_bfloat16* ob, __nv_bfloat16* rob, int64_t T, int64_t D, float eps, int gemma,
+                             uint8_t* qp, float* qs, cudaStream_t cs) {
+  if (D <= 2048) rmsnorm_vec_kernel<1, QA><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
+  else if (D <= 4096) rmsnorm_vec_kernel<2, QA><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
+  else rmsnorm_vec_kernel<4, QA><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -256,9 +305,9 @@ int actune_harness_rmsnorm(const void* x, const void* residual, const void* weig
     const auto* wb = reinterpret_cast<const __nv_bfloat16*>(weight);
     auto* ob = reinterpret_cast<__nv_bfloat16*>(out);
     auto* rob = reinterpret_cast<__nv_bfloat16*>(residual_out);
-    if (D <= 2048) rmsnorm_vec_kernel<1><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma);
-    else if (D <= 4096) rmsnorm_vec_kernel<2><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma);
-    else rmsnorm_vec_kernel<4><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma);
+    if (D <= 2048) rmsnorm_vec_kernel<1, 0><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, nullptr, nullptr);
+    else if (D <= 4096) rmsnorm_vec_kernel<2, 0><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, nullptr, nullptr);
+    else rmsnorm_vec_kernel<4, 0><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, nullptr, nullptr);
     return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
   }
   rmsnorm_kernel<<<(unsigned)T, 256, D * sizeof(float), reinterpret_cast<cudaStream_t>(stream)>>>(
@@ -288,12 +337,53 @@ int actune_harness_gated_act(const void* gu, void* out, int64_t T, int64_t I, in
   if (T < 0 || I <= 0 || gu == nullptr || out == nullptr) return ACTUNE_ERR_INVALID_VALUE;
   if (T == 0) return ACTUNE_OK;
   if (I % 8 == 0 && aligned16(gu) && aligned16(out)) {
-    gated_act_vec_kernel<<<grid_for(T * I / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(out), (int)T, (int)I, gelu);
+    gated_act_vec_kernel<0><<<grid_for(T * I / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(out), (int)T, (int)I, gelu,
+        nullptr, nullptr);
     return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
   }
   gated_act_kernel<<<grid_for(T * I), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(out), (int)T, (int)I, gelu);
+  return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
+int actune_harness_rmsnorm_q(const void* x, const void* residual, const void* weight, void* out, void* residual_out,
+                             int64_t T, int64_t D, float eps, int gemma, int A, uint8_t* packed, float* scales,
+                             void* stream) {
+  if (T < 0 || D <= 0 || D > 8192 || D % 256 || x == nullptr || weight == nullptr || out == nullptr ||
+      packed == nullptr || scales == nullptr || (residual != nullptr && residual_out == nullptr) ||
+      (A != 2 && A != 4 && A != 8))
+    return ACTUNE_ERR_INVALID_VALUE;
+  if (T == 0) return ACTUNE_OK;
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(out) || !aligned16(packed) || !aligned16(scales) ||
+      (residual != nullptr && (!aligned16(residual) || !aligned16(residual_out))))
+    return ACTUNE_ERR_MISALIGNED;
+  const auto* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  const auto* rb = reinterpret_cast<const __nv_bfloat16*>(residual);
+  const auto* wb = reinterpret_cast<const __nv_bfloat16*>(weight);
+  auto* ob = reinterpret_cast<__nv_bfloat16*>(out);
+  auto* rob = reinterpret_cast<__nv_bfloat16*>(residual_out);
+  auto* cs = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = A == 8 ? launch_rmsnorm_q<8>(xb, rb, wb, ob, rob, T, D, eps, gemma, packed, scales, cs)
+                : A == 4 ? launch_rmsnorm_q<4>(xb, rb, wb, ob, rob, T, D, eps, gemma, packed, scales, cs)
+                         : launch_rmsnorm_q<2>(xb, rb, wb, ob, rob, T, D, eps, gemma, packed, scales, cs);
+  return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
+int actune_harness_gated_act_q(const void* gu, void* out, int64_t T, int64_t I, int gelu, int A, uint8_t* packed,
+                               float* scales, void* stream) {
+  if (T < 0 || I <= 0 || I % 64 || gu == nullptr || out == nullptr || packed == nullptr || scales == nullptr ||
+      (A != 2 && A != 4 && A != 8))
+    return ACTUNE_ERR_INVALID_VALUE;
+  if (T == 0) return ACTUNE_OK;
+  if (!aligned16(gu) || !aligned16(out) || !aligned16(packed) || !aligned16(scales)) return ACTUNE_ERR_MISALIGNED;
+  const auto* g = reinterpret_cast<const __nv_bfloat16*>(gu);
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out);
+  auto* cs = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = grid_for(T * I / 8);
+  if (A == 8) gated_act_vec_kernel<8><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
+  else if (A == 4) gated_act_vec_kernel<4><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
+  else gated_act_vec_kernel<2><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
   return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
 }
 

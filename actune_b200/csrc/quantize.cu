@@ -57,9 +57,6 @@ __device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
 template <int A, typename T>
 __global__ void __launch_bounds__(256) quantize_group64_kernel(const T* __restrict__ x, uint8_t* __restrict__ packed,
                                                                float* __restrict__ scales, int64_t groups) {
-  constexpr float kPositive = float((1 << (A - 1)) - 1);
-  constexpr float kLo = -float(1 << (A - 1));
-  constexpr int kMask = (1 << A) - 1;
   const int lane = threadIdx.x & 31;
   const int seg = lane >> 3, l8 = lane & 7;
   const int64_t warp_global = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -74,31 +71,10 @@ __global__ void __launch_bounds__(256) quantize_group64_kernel(const T* __restri
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = 0.f;
     }
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    uint32_t word[2];
+    const float scale = quantize_lane8<A>(v, word);
     if (!live) continue;
-    const float scale = __fdiv_rn(fmaxf(amax, 1e-8f), kPositive);
-    uint32_t word[2] = {0u, 0u};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float q = rintf(__fdiv_rn(v[i], scale));
-      q = fminf(fmaxf(q, kLo), kPositive);
-      const uint32_t field = (uint32_t)((int)q) & kMask;
-      const int bit = i * A;  // bit position within this lane's 8*A-bit run
-      word[bit >> 5] |= field << (bit & 31);
-    }
-    uint8_t* dst = packed + g * (64 * A / 8) + l8 * A;
-    if constexpr (A == 8) {
-      *reinterpret_cast<uint2*>(dst) = make_uint2(word[0], word[1]);
-    } else if constexpr (A == 4) {
-      *reinterpret_cast<uint32_t*>(dst) = word[0];
-    } else {
-      *reinterpret_cast<uint16_t*>(dst) = (uint16_t)word[0];
-    }
+    store_lane_codes<A>(packed + g * (64 * A / 8) + l8 * A, word);
     if (l8 == 0) scales[g] = scale;
   }
 }

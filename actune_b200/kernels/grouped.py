@@ -48,11 +48,37 @@ def shared_activation_scope(enabled=True):
         _SHARED.reset(token)
 
 
+def _version(t):
+    # Inference-mode tensors carry no version counter: within one scope they are
+    # matched by storage, shape, dtype and width alone (an in-place update of such
+    # an input between two projections of the same scope is not detected).
+    return -1 if t.is_inference() else t._version
+
+
+def shared_activation_active():
+    """True inside an enabled shared_activation_scope."""
+    return _SHARED.get() is not None
+
+
+def share_quantized(flat, bits, packed, scales):
+    """Offer already packed activations of `flat` (bit-identical to what
+    ``ops.quantize_group64(flat, bits)`` returns) to the active shared activation
+    scope, so the next projection reading `flat` reuses them.  No-op outside one."""
+    cache = _SHARED.get()
+    if cache is None:
+        return False
+    key = (flat.data_ptr(), _version(flat), tuple(flat.shape), flat.dtype, flat.device, bits)
+    cache.append((key, flat, packed, scales))
+    if len(cache) > _SHARED_CAPACITY:
+        cache.pop(0)
+    return True
+
+
 def _quantize_shared(flat, bits):
     cache = _SHARED.get()
     if cache is None:
         return ops.quantize_group64(flat, bits)
-    key = (flat.data_ptr(), flat._version, tuple(flat.shape), flat.dtype, flat.device, bits)
+    key = (flat.data_ptr(), _version(flat), tuple(flat.shape), flat.dtype, flat.device, bits)
     for entry_key, _, packed, scales in cache:
         if entry_key == key:
             return packed, scales

@@ -283,7 +283,9 @@ def ours(args):
 
     torch.manual_seed(1234 + rank)
     model, runtime = make_oft_policy(layers=args.layers, tokens=TOKENS, seed=rank)
-    policy = GraphReplay(model.forward, runtime.modules, max_graphs=12)
+    # shared_a8: the glue kernels hand each projection its packed input (one quantizer
+    # pass per activation instead of a separate launch per projection).
+    policy = GraphReplay(model.forward, runtime.modules, shared_a8=True, max_graphs=12)
     policy.enabled = True
     cycle = config_cycle()
     host_in = torch.randn(TOKENS, HIDDEN, generator=torch.Generator().manual_seed(7 + rank)).bfloat16().pin_memory()

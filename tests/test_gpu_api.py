@@ -288,7 +288,53 @@ def test_harness_glue_kernels(d):
         assert torch.equal(qkv[:, 3 * dh:], before[:, 3 * dh:])  # v untouched
 
 
+@pytest.mark.parametrize("bits", [2, 4, 8])
+def test_glue_kernels_quantize_like_the_quantizer(bits):
+    """RMSNorm and the gated activation with the quantizing epilogue produce the
+    bf16 output of the plain kernels and, bit for bit, the packed codes and scales
+    of actune_quantize_group64 on that output."""
+    import ctypes
+    from actune_b200 import harness as H
+    from actune_b200 import ops
+    torch.manual_seed(bits)
+    L = H._hlib()
+    for d, gemma, with_res in ((256, False, True), (4096, False, False), (2048, True, True)):
+        x = torch.randn(9, d, device="cuda", dtype=torch.bfloat16) * 3
+        r = torch.randn(9, d, device="cuda", dtype=torch.bfloat16) if with_res else None
+        w = torch.randn(d, device="cuda", dtype=torch.bfloat16)
+        ref_out, ref_res = H.rmsnorm(x, w, 1e-5, r, gemma)
+        out = torch.empty_like(x)
+        res_out = torch.empty_like(x) if with_res else None
+        packed = torch.empty(9, d * bits // 8, device="cuda", dtype=torch.uint8)
+        scales = torch.empty(9, d // 64, device="cuda", dtype=torch.float32)
+        rc = L.actune_harness_rmsnorm_q(H._p(x), H._p(r), H._p(w), H._p(out), H._p(res_out), 9, d,
+                                        ctypes.c_float(1e-5), int(gemma), bits, H._p(packed), H._p(scales), H._s(x))
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref_out)
+        if with_res:
+            assert torch.equal(res_out, ref_res)
+        qp, qs = ops.quantize_group64(out, bits)
+        assert torch.equal(packed, qp) and torch.equal(scales, qs)
+    for inter, gelu in ((512, False), (11008, False), (1024, True)):
+        gu = torch.randn(7, 2 * inter, device="cuda", dtype=torch.bfloat16)
+        ref = H.gated_act(gu, gelu)
+        out = torch.empty_like(ref)
+        packed = torch.empty(7, inter * bits // 8, device="cuda", dtype=torch.uint8)
+        scales = torch.empty(7, inter // 64, device="cuda", dtype=torch.float32)
+        rc = L.actune_harness_gated_act_q(H._p(gu), H._p(out), 7, inter, int(gelu), bits, H._p(packed),
+                                          H._p(scales), H._s(gu))
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+        qp, qs = ops.quantize_group64(out, bits)
+        assert torch.equal(packed, qp) and torch.equal(scales, qs)
+
+
 def test_small_oft_backbone_graph_vs_eager():
+    """Graph replay (shared activation scope: the glue kernels hand the next
+    projection its packed input) is bit-identical to eager calls (no scope: every
+    projection quantizes its own input)."""
     from actune_b200.graph import GraphReplay
     from actune_b200.harness import OFTBackbone, build_w4a8_bank
     from actune_b200.layers import install_bank
@@ -302,10 +348,11 @@ def test_small_oft_backbone_graph_vs_eager():
     for q in ("q00", "q11"):
         with precision_profile(q), torch.inference_mode():
             eager[q] = model(x).clone()
-    policy = GraphReplay(model.forward, runtime.modules)
-    policy.enabled = True
-    for q in ("q00", "q11", "q00"):
-        with precision_profile(q), torch.inference_mode():
-            assert torch.equal(policy(x), eager[q])
+    for shared in (False, True):
+        policy = GraphReplay(model.forward, runtime.modules, shared_a8=shared)
+        policy.enabled = True
+        for q in ("q00", "q11", "q00"):
+            with precision_profile(q), torch.inference_mode():
+                assert torch.equal(policy(x), eager[q])
+        policy.release()
     assert not torch.equal(eager["q00"], eager["q11"])
-    policy.release()
