@@ -285,4 +285,58 @@ int oracle_weight_codes(const float* weight, int64_t N, int64_t K, int W, int A,
     return ORACLE_OK;
 }
 
+/* ---- tokenwise backends (reference actune/kernels/w4a8_triton.py,
+ * w8a8_triton.py, w2a8_triton.py) --------------------------------------------
+ *
+ * Per-row dynamic INT8 activation quantizer, w4a8_triton.py:161-201:
+ *   scale = max(row absmax, 1e-8) * fp32(1/127)   -- a multiply by the binary32
+ *           reciprocal, as torch lowers CUDA tensor/scalar division (the
+ *           reference reproduces that on purpose, w4a8_triton.py:179-184)
+ *   code  = clamp(rint(x / scale), -128, 127)      -- IEEE division, RNE */
+int oracle_quantize_rows_a8(const uint16_t* x, int64_t M, int64_t K, int8_t* codes, float* scales) {
+    if (M < 0 || K <= 0) return 1;
+    const float recip = 1.0f / 127.0f;
+    for (int64_t m = 0; m < M; ++m) {
+        const uint16_t* row = x + m * K;
+        float amax = 0.0f;
+        for (int64_t k = 0; k < K; ++k) {
+            const float v = fabsf(bf16_to_f32(row[k]));
+            if (v > amax) amax = v;
+        }
+        const float scale = (amax > 1e-8f ? amax : 1e-8f) * recip;
+        scales[m] = scale;
+        for (int64_t k = 0; k < K; ++k) {
+            float q = rintf(bf16_to_f32(row[k]) / scale);
+            if (q < -128.0f) q = -128.0f;
+            if (q > 127.0f) q = 127.0f;
+            codes[m * K + k] = (int8_t)(int)q;
+        }
+    }
+    return 0;
+}
+
+/* Tokenwise linear, w4a8_triton.py:57-114 (and the W8/W2 kernels): exact int32
+ * dot over all of K, then out = float(acc) * as[m]; out *= ws[n]; out += bias[n]
+ * in that order (fma_mode 1 fuses the last multiply and add, as GPU compilers
+ * do; 0 rounds twice).  codes is [N, K] int8. */
+int oracle_tokenwise_linear(const int8_t* a, const float* as, const int8_t* codes, const float* ws,
+                            const float* bias, int64_t M, int64_t N, int64_t K, int fma_mode, float* out) {
+    if (M < 0 || N < 0 || K <= 0) return 1;
+    for (int64_t m = 0; m < M; ++m) {
+        for (int64_t n = 0; n < N; ++n) {
+            int64_t acc = 0;
+            for (int64_t k = 0; k < K; ++k) acc += (int64_t)a[m * K + k] * (int64_t)codes[n * K + k];
+            const float t = (float)(int32_t)acc * as[m];
+            float y;
+            if (bias) {
+                y = fma_mode ? fmaf(t, ws[n], bias[n]) : t * ws[n] + bias[n];
+            } else {
+                y = t * ws[n];
+            }
+            out[m * N + n] = y;
+        }
+    }
+    return 0;
+}
+
 int oracle_abi_version(void) { return 1; }

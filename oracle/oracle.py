@@ -52,6 +52,8 @@ def lib():
         L.oracle_group_dots.argtypes = [p, p, i64, i64, i64, i32, i32, p]
         L.oracle_packed_linear.argtypes = [p, p, p, p, p, i64, i64, i64, i32, i32, i32, p]
         L.oracle_weight_codes.argtypes = [p, i64, i64, i32, i32, p, p, p]
+        L.oracle_quantize_rows_a8.argtypes = [p, i64, i64, p, p]
+        L.oracle_tokenwise_linear.argtypes = [p, p, p, p, p, i64, i64, i64, i32, p]
         L.oracle_f32_to_bf16_array.argtypes = [p, p, i64]
         L.oracle_f32_to_bf16_array.restype = None
         _LIB = L
@@ -131,6 +133,34 @@ def weight_codes(weight, W: int, A: int, clip=None):
     scale = np.zeros((N,), np.float32)
     _check(lib().oracle_weight_codes(_ptr(weight), N, K, W, A, _ptr(c), _ptr(codes), _ptr(scale)))
     return codes, scale
+
+
+def quantize_rows_a8(x_bf16_bits):
+    """Per-row dynamic INT8 codes [M, K] int8 and scales [M] f32 of a bf16 matrix
+    (given as uint16 bits), reference w4a8_triton.py:161-201."""
+    x = np.ascontiguousarray(x_bf16_bits, np.uint16)
+    M, K = x.shape
+    codes = np.empty((M, K), np.int8)
+    scales = np.empty(M, np.float32)
+    _check(lib().oracle_quantize_rows_a8(_ptr(x), M, K, _ptr(codes), _ptr(scales)))
+    return codes, scales
+
+
+def tokenwise_linear(a, a_scale, codes, w_scale, bias, fma: bool = True):
+    """Tokenwise W{2,4,8}A8 linear [M, N] f32 from int8 activations [M, K], row
+    scales [M], weight codes [N, K] int8 and row scales [N] (reference
+    w4a8_triton.py:57-114)."""
+    a = np.ascontiguousarray(a, np.int8)
+    codes = np.ascontiguousarray(codes, np.int8)
+    a_scale = np.ascontiguousarray(a_scale, np.float32)
+    w_scale = np.ascontiguousarray(w_scale, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    M, K = a.shape
+    N = codes.shape[0]
+    out = np.empty((M, N), np.float32)
+    _check(lib().oracle_tokenwise_linear(_ptr(a), _ptr(a_scale), _ptr(codes), _ptr(w_scale), _ptr(b), M, N, K,
+                                         1 if fma else 0, _ptr(out)))
+    return out
 
 
 def to_bf16_bits(x):

@@ -93,3 +93,27 @@ def test_bf16_rounding_is_rne():
     import torch
     ref = torch.from_numpy(vals).bfloat16().view(torch.int16).numpy().view(np.uint16)
     assert np.array_equal(bits, ref)
+
+
+# ---------------------------------------------------------------------------- tokenwise backends
+@pytest.fixture(scope="module")
+def tokenwise():
+    return np.load(GOLDEN / "tokenwise.npz")
+
+
+@pytest.mark.parametrize("w", [4, 8, 2])
+@pytest.mark.parametrize("si", [0, 1, 2])
+def test_tokenwise_matches_reference(tokenwise, w, si):
+    """Per-row A8 quantizer (reciprocal-multiply scale), the W{4,8,2} codebooks and
+    the full-K int32 GEMM with its fp32 epilogue, against the reference's
+    W{4,8,2}A8TritonLinear kernels run under the Triton interpreter."""
+    g, key = tokenwise, f"w{w}_s{si}"
+    codes_a, scale = O.quantize_rows_a8(g[f"{key}_x"])
+    assert bits_equal(codes_a, g[f"{key}_act"]) and bits_equal(scale, g[f"{key}_scale"])
+    wq, ws = O.weight_codes(O.bf16_bits_to_f32(g[f"{key}_weight"]), w, 8)
+    assert bits_equal(wq, g[f"{key}_codes"]) and bits_equal(ws, g[f"{key}_ws"])
+    bias = O.bf16_bits_to_f32(g[f"{key}_bias"]) if f"{key}_bias" in g else None
+    y = O.tokenwise_linear(codes_a, scale, wq, ws, bias, fma=False)  # interpreter: separate multiply and add
+    assert bits_equal(y, g[f"{key}_out"])
+    yf = O.tokenwise_linear(codes_a, scale, wq, ws, bias, fma=True)
+    assert float(np.max(np.abs(yf - y))) <= 1e-6 * (float(np.abs(y).max()) + 1e-30)
