@@ -290,6 +290,45 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   return cuda_status(e);
 }
 
+int run_tokenwise(const int8_t* a, const float* a_scale, const uint8_t* w, const float* w_scale, const void* bias,
+                  int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K, int W, int variant,
+                  cudaStream_t stream) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != ACTUNE_OK) return rc;
+  if (M == 0 || N == 0) return ACTUNE_OK;
+  if (!aligned(a, 16) || !aligned(w, 16)) return ACTUNE_ERR_MISALIGNED;
+  const int bn = pick_bn(variant, M, N, g_devices[dev].num_sms);
+  CUtensorMap ta, tw;
+  rc = encode_map(&ta, a, M, K, 128, 128, Swz::B128);
+  if (rc != ACTUNE_OK) return rc;
+  rc = encode_map(&tw, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn, W == 8 ? Swz::B128 : Swz::None);
+  if (rc != ACTUNE_OK) return rc;
+  GemmParams p{};
+  p.act_scale = a_scale;
+  p.w_scale = w_scale;
+  p.bias = bias;
+  p.out = out;
+  p.dots = nullptr;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.G = (int)((K + 63) / 64);  // stages of 128 codes; the zero fill past K adds nothing
+  p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
+  p.out_dtype = out_dtype;
+  p.out_vec_ok = (N % 8 == 0) && aligned(out, 16);
+  cudaError_t e = cudaErrorInvalidValue;
+#define ACTUNE_TW(WW)                                                              \
+  if (W == WW) {                                                                   \
+    e = bn == 32   ? launch_group64_tokenwise<WW, 32>(ta, tw, p, stream)           \
+        : bn == 64 ? launch_group64_tokenwise<WW, 64>(ta, tw, p, stream)           \
+                   : launch_group64_tokenwise<WW, 128>(ta, tw, p, stream);         \
+  }
+  ACTUNE_TW(2) ACTUNE_TW(4) ACTUNE_TW(8)
+#undef ACTUNE_TW
+  return cuda_status(e);
+}
+
 }  // namespace
 }  // namespace actune
 
@@ -346,6 +385,40 @@ int actune_packed_linear(const uint8_t* a, const float* a_scale, const uint8_t* 
   const int odt = out_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (out_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
   return run_gemm(a, a_scale, w, w_scale, bias, bdt, out, odt, nullptr, M, N, K, W, A, variant,
                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+int actune_quantize_rows_a8(const void* x, int x_dtype, int64_t M, int64_t K, int8_t* codes, float* scales,
+                            void* stream) {
+  if (!valid_float_dtype(x_dtype) || M < 0 || K <= 0 || K % 8) return ACTUNE_ERR_INVALID_VALUE;
+  if (M > 0 && (x == nullptr || codes == nullptr || scales == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != ACTUNE_OK) return rc;
+  if (M == 0) return ACTUNE_OK;
+  if (!aligned(x, 16) || !aligned(codes, 8) || !aligned(scales, 4)) return ACTUNE_ERR_MISALIGNED;
+  const int dt = x_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (x_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
+  return cuda_status(launch_quantize_rows_a8(x, dt, M, K, codes, scales, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int actune_tokenwise_linear(const int8_t* a, const float* a_scale, const uint8_t* w, const float* w_scale,
+                            const void* bias, int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                            int W, int variant, void* stream) {
+  if (!valid_bits(W) || K <= 0 || K % 64 || K > (int64_t(1) << 24) || M < 0 || N < 0 || M >= (int64_t(1) << 31) ||
+      N >= (int64_t(1) << 31))
+    return ACTUNE_ERR_INVALID_VALUE;
+  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_BN128) return ACTUNE_ERR_INVALID_VALUE;
+  if (bias != nullptr && !valid_float_dtype(bias_dtype)) return ACTUNE_ERR_INVALID_VALUE;
+  if (M > 0 && N > 0 && (a == nullptr || a_scale == nullptr || w == nullptr || w_scale == nullptr || out == nullptr))
+    return ACTUNE_ERR_INVALID_VALUE;
+  if (!aligned(a_scale, 4) || !aligned(w_scale, 4) || !aligned(out, dtype_size(out_dtype)) ||
+      (bias != nullptr && !aligned(bias, dtype_size(bias_dtype))))
+    return ACTUNE_ERR_MISALIGNED;
+  const int bdt = bias == nullptr ? kDtNone
+                                  : (bias_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16
+                                                                     : (bias_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32));
+  const int odt = out_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (out_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
+  return run_tokenwise(a, a_scale, w, w_scale, bias, bdt, out, odt, M, N, K, W, variant,
+                       reinterpret_cast<cudaStream_t>(stream));
 }
 
 int actune_packed_linear_dots(const uint8_t* a, const uint8_t* w, int32_t* dots, int64_t M, int64_t N, int64_t K,

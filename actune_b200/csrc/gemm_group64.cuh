@@ -177,7 +177,10 @@ __device__ __forceinline__ void store_dots(const GemmParams& p, int m, int col, 
   }
 }
 
-template <int W, int A, int BN, bool DOTS>
+// TW (tokenwise backends): one full-K int32 accumulator per tile instead of one per
+// 64-group; the epilogue reads it once, converts it exactly (round to nearest) and
+// applies the per-token scale (p.act_scale[m]), then ws / bias as below.
+template <int W, int A, int BN, bool DOTS, bool TW = false>
 __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
     group64_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
                         const GemmParams p) {
@@ -314,11 +317,27 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
           const int q = j & 1;
           uint64_t* ready = C::CONVERT ? &full_op[j] : &full_raw[j];
           if (!mbar_wait(ready, ph, kSiteMmaFull) ||
-              !mbar_wait(&acc_empty[pr], ((it / C::NPAIR) & 1) ^ 1, kSiteMmaAcc)) {
+              (!TW && !mbar_wait(&acc_empty[pr], ((it / C::NPAIR) & 1) ^ 1, kSiteMmaAcc))) {
             ok = false;
             break;
           }
           tc_fence_after();
+          if constexpr (TW) {
+            // Every K slice of every stage into one accumulator.
+            mma_i8(dacc[0][0], da[q][0], dw[q][0], idesc, it > 0 ? 1u : 0u);
+            mma_i8(dacc[0][0], da[q][1], dw[q][1], idesc, 1u);
+            mma_i8(dacc[0][0], da[q][2], dw[q][2], idesc, 1u);
+            mma_i8(dacc[0][0], da[q][3], dw[q][3], idesc, 1u);
+            if (it == n_iters - 1) mma_commit_u32(bacc[0]);
+            mma_commit_u32(bempty[j]);
+            const int jn = (j + 1) % S;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              da[q ^ 1][k] = desc_a0 + kStageStep * jn + 2 * k;
+              dw[q ^ 1][k] = desc_w0 + kStageStep * jn + 2 * k;
+            }
+            continue;
+          }
           // Always both groups: past the end of K (odd G) the tiles are the
           // TMA's zero fill, the dots are 0 and the epilogue gives them scale 0.
           mma_i8(dacc[pr][0], da[q][0], dw[q][0], idesc, 0u);  // group 2it:   K bytes 0..31
@@ -386,7 +405,27 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
     auto scale_at = [&](int g) -> float { return (load_scales && g < G) ? __ldg(as_row + g) : 0.f; };
     uint32_t ra[H], rb[H];
     bool ok = true;
-    if (!warp_live) {
+    if constexpr (TW) {
+      // One wait for the whole-K accumulator, then y = float(acc) * 2^-SHIFT (exact:
+      // a power of two) * as[m], stored in the accumulator registers for the final
+      // ws / bias step below.
+      ok = mbar_wait(&acc_full[0], 0, kSiteEpilogue);
+      if (ok) {
+        tc_fence_after();
+        const float as_m = (m < p.M) ? __ldg(p.act_scale + m) : 0.f;
+#pragma unroll
+        for (int part = 0; part < C::COLS / H; ++part) {
+          tmem_ld<H>(lane_base + part * H, ra);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < H / 2; ++j) {
+            const float f0 = __int2float_rn((int)ra[2 * j]) * shift_scale;
+            const float f1 = __int2float_rn((int)ra[2 * j + 1]) * shift_scale;
+            acc[part * (H / 2) + j] = make_float2(f0 * as_m, f1 * as_m);
+          }
+        }
+      }
+    } else if (!warp_live) {
       // No valid token row in this warp: only keep the accumulator handshake.
       for (int it = 0; it < n_iters; ++it) {
         const int pr = it % C::NPAIR;
@@ -525,5 +564,9 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
 template <int W, int A, int BN>
 cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
                                 cudaStream_t stream);
+// Tokenwise mode (A = 8 codes, per-token act_scale [M]).
+template <int W, int BN>
+cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
+                                     cudaStream_t stream);
 
 }  // namespace actune

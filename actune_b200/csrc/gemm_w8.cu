@@ -23,6 +23,29 @@ cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm
   return cudaGetLastError();
 }
 
+template <int W, int BN>
+cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
+                                     cudaStream_t stream) {
+  using C = Group64Cfg<W, 8, BN>;
+  auto kernel = group64_gemm_kernel<W, 8, BN, false, true>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const dim3 grid((p.M + C::BM - 1) / C::BM, (p.N + BN - 1) / BN);
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
+  return cudaGetLastError();
+}
+
+template cudaError_t launch_group64_tokenwise<8, 32>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+template cudaError_t launch_group64_tokenwise<8, 64>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+template cudaError_t launch_group64_tokenwise<8, 128>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+
 #define ACTUNE_INST(A, BN)                                                                                  \
   template cudaError_t launch_group64_gemm<8, A, BN>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, \
                                                      cudaStream_t);

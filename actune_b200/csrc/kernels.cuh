@@ -6,6 +6,9 @@
 
 namespace actune {
 
+// Per-row dynamic INT8 quantizer of the tokenwise backends (K % 8 == 0, 16-byte aligned x).
+cudaError_t launch_quantize_rows_a8(const void* x, int dtype, int64_t M, int64_t K, int8_t* codes, float* scales,
+                                    cudaStream_t stream);
 cudaError_t launch_quantize_group64(const void* x, int dtype, int64_t groups, int A, uint8_t* packed, float* scales,
                                     int num_sms, cudaStream_t stream);
 cudaError_t launch_weight_codes(const void* w, int dtype, int64_t N, int64_t K, int W, int A, const float* clip,

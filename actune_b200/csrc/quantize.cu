@@ -228,6 +228,93 @@ cudaError_t launch_quantize_group64(const void* x, int dtype, int64_t groups, in
   }
 }
 
+// Per-row dynamic INT8 activation quantizer of the tokenwise backends, restating
+// actune/kernels/w4a8_triton.py:161-201: scale = max(row absmax, 1e-8) * fp32(1/127)
+// (a multiply by the binary32 reciprocal, which is what torch computes for a CUDA
+// tensor divided by a scalar and what the reference reproduces on purpose), then
+// code = clamp(rint(x / scale), -128, 127) with IEEE division.  One CTA per row;
+// each thread holds up to CPT chunks of 8 values in registers between the absmax
+// and the quantizing pass (CPT == 0: K beyond the register cache, read twice).
+template <typename T, int CPT>
+__global__ void __launch_bounds__(256) quantize_rows_a8_kernel(const T* __restrict__ x, int8_t* __restrict__ codes,
+                                                               float* __restrict__ scales, int64_t K) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * K;
+  constexpr int C = CPT > 0 ? CPT : 1;
+  float v[C][8];
+  float amax = 0.f;
+  if constexpr (CPT > 0) {
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+      const int64_t i = ((int64_t)threadIdx.x + c * 256) * 8;
+      if (i < K) {
+        load8<T>(xr + i, v[c]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[c][k]));
+      }
+    }
+  } else {
+    for (int64_t i = (int64_t)threadIdx.x * 8; i < K; i += 256 * 8) {
+      load8<T>(xr + i, v[0]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[0][k]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  float a = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) a = fmaxf(a, red[w]);
+  const float recip = 1.0f / 127.0f;  // binary32 reciprocal, folded at compile time
+  const float scale = fmaxf(a, 1e-8f) * recip;
+  if (threadIdx.x == 0) scales[row] = scale;
+  auto emit = [&](const float (&vv)[8], int64_t i) {
+    uint32_t word[2] = {0u, 0u};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float q = rintf(__fdiv_rn(vv[k], scale));
+      q = fminf(fmaxf(q, -128.f), 127.f);
+      word[k >> 2] |= ((uint32_t)((int)q) & 0xFFu) << ((k & 3) * 8);
+    }
+    *reinterpret_cast<uint2*>(codes + row * K + i) = make_uint2(word[0], word[1]);
+  };
+  if constexpr (CPT > 0) {
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) {
+      const int64_t i = ((int64_t)threadIdx.x + c * 256) * 8;
+      if (i < K) emit(v[c], i);
+    }
+  } else {
+    for (int64_t i = (int64_t)threadIdx.x * 8; i < K; i += 256 * 8) {
+      load8<T>(xr + i, v[0]);
+      emit(v[0], i);
+    }
+  }
+}
+
+template <typename T>
+static cudaError_t launch_rows_t(const T* x, int64_t M, int64_t K, int8_t* codes, float* scales, cudaStream_t s) {
+  const unsigned grid = (unsigned)M;
+  if (K <= 2048) quantize_rows_a8_kernel<T, 1><<<grid, 256, 0, s>>>(x, codes, scales, K);
+  else if (K <= 4096) quantize_rows_a8_kernel<T, 2><<<grid, 256, 0, s>>>(x, codes, scales, K);
+  else if (K <= 8192) quantize_rows_a8_kernel<T, 4><<<grid, 256, 0, s>>>(x, codes, scales, K);
+  else quantize_rows_a8_kernel<T, 0><<<grid, 256, 0, s>>>(x, codes, scales, K);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows_a8(const void* x, int dtype, int64_t M, int64_t K, int8_t* codes, float* scales,
+                                    cudaStream_t stream) {
+  if (M == 0) return cudaSuccess;
+  switch (dtype) {
+    case kDtBF16: return launch_rows_t(reinterpret_cast<const __nv_bfloat16*>(x), M, K, codes, scales, stream);
+    case kDtF16: return launch_rows_t(reinterpret_cast<const __half*>(x), M, K, codes, scales, stream);
+    default: return launch_rows_t(reinterpret_cast<const float*>(x), M, K, codes, scales, stream);
+  }
+}
+
 cudaError_t launch_weight_codes(const void* w, int dtype, int64_t N, int64_t K, int W, int A, const float* clip,
                                 int8_t* codes, float* scale, cudaStream_t stream) {
   if (N == 0) return cudaSuccess;

@@ -23,6 +23,7 @@ from unittest.mock import patch
 
 import torch
 
+from .kernels._tokenwise import shared_a8_cache_scope
 from .kernels.grouped import shared_activation_scope
 from .precision import active_precision_profile
 
@@ -62,7 +63,8 @@ class GraphReplay:
             # Clone: callers may update such constants in place (e.g. a time step).
             return self.constants[key].clone()
 
-        with shared_activation_scope(self.shared_a8), patch.object(torch, "tensor", constant):
+        with shared_activation_scope(self.shared_a8), shared_a8_cache_scope(enabled=self.shared_a8), \
+                patch.object(torch, "tensor", constant):
             yield
 
     def key(self, leaves, tree):

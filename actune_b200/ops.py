@@ -92,6 +92,45 @@ def packed_linear(a, a_scale, w, w_scale, bias, K: int, W: int, A: int, out_dtyp
     return out
 
 
+def quantize_rows_a8(x, codes=None, scales=None):
+    """Per-row dynamic INT8 activations of x [M, K]: (codes int8 [M, K], scales f32 [M]),
+    scale = max(row absmax, 1e-8) * fp32(1/127), reference w4a8_triton.py:161-201."""
+    _require(x.dim() == 2, "x must be 2-D [M, K]")
+    m, k = x.shape
+    _require(k % 8 == 0, "K must be a multiple of 8")
+    if codes is None:
+        codes = torch.empty((m, k), device=x.device, dtype=torch.int8)
+    if scales is None:
+        scales = torch.empty(m, device=x.device, dtype=torch.float32)
+    dev = _cuda_contig(x, codes, scales)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().actune_quantize_rows_a8(_ptr(x), dtype_code(x.dtype), m, k, _ptr(codes), _ptr(scales),
+                                                      _stream(dev)), "quantize_rows_a8")
+    return codes, scales
+
+
+def tokenwise_linear(a, a_scale, w_rows, w_scale, bias, K: int, W: int, out_dtype=torch.bfloat16,
+                     variant: int = _lib.VARIANT_AUTO, out: torch.Tensor | None = None):
+    """out[M, N] = float(a @ codes.T) * a_scale[:, None] * w_scale (+ bias) for int8
+    activations [M, K] and weight codes packed as rows [N, K*W/8]."""
+    _require(a.dim() == 2 and w_rows.dim() == 2, "rank mismatch")
+    m, n = a.shape[0], w_rows.shape[0]
+    _require(a.dtype == torch.int8 and w_rows.dtype == torch.uint8, "int8 activations and uint8 weight rows required")
+    _require(a.shape[1] == K and w_rows.shape[1] == K * W // 8, "packed shape mismatch")
+    _require(a_scale.numel() == m and w_scale.numel() == n, "scale shape mismatch")
+    if bias is not None and bias.numel() == 0:
+        bias = None
+    if out is None:
+        out = torch.empty((m, n), device=a.device, dtype=out_dtype)
+    dev = _cuda_contig(a, a_scale, w_rows, w_scale, bias, out)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().actune_tokenwise_linear(
+            _ptr(a), _ptr(a_scale), _ptr(w_rows), _ptr(w_scale), _ptr(bias),
+            _lib.DTYPE_NONE if bias is None else dtype_code(bias.dtype), _ptr(out), dtype_code(out.dtype),
+            m, n, K, W, int(variant), _stream(dev)), "tokenwise_linear")
+    return out
+
+
 def packed_linear_dots(a, w, K: int, W: int, A: int, variant: int = _lib.VARIANT_AUTO):
     """Exact per-group int32 dots [M, N, K/64] from the tensor-core kernel (debug export)."""
     m, n = a.shape[0], w.shape[0]

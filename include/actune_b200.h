@@ -91,6 +91,27 @@ int actune_packed_linear(const uint8_t* a, const float* a_scale, const uint8_t* 
                          const void* bias, int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
                          int W, int A, int variant, void* stream);
 
+/* Tokenwise backends (replace actune/kernels/w4a8_triton.py, w8a8_triton.py,
+ * w2a8_triton.py).
+ *
+ * actune_quantize_rows_a8: per-row dynamic INT8 activations of x [M, K] (bf16 /
+ * f16 / f32, K % 8 == 0, 16-byte aligned): scale[m] = max(row absmax, 1e-8) *
+ * fp32(1/127), codes = clamp(rint(x / scale), -128, 127); replaces
+ * _quantize_rows_kernel, w4a8_triton.py:161-201.
+ *
+ * actune_tokenwise_linear: out[M, N] = float(sum_k a[m,k] w[n,k]) * a_scale[m] *
+ * w_scale[n] (+ bias[n], fused with the last multiply) for int8 activations
+ * [M, K] and weight codes of W bits packed as rows [N, K*W/8] (the layout of
+ * actune_pack_rows; the Python modules derive it from the reference's K-major
+ * buffers).  K % 64 == 0.  variant: AUTO or BN32/BN64/BN128.  Replaces
+ * _w4a8_gemm_kernel (w4a8_triton.py:57-114), _w8a8_gemm_kernel
+ * (w8a8_triton.py:22-77), _w2a8_gemm_kernel (w2a8_triton.py:25-112). */
+int actune_quantize_rows_a8(const void* x, int x_dtype, int64_t M, int64_t K, int8_t* codes, float* scales,
+                            void* stream);
+int actune_tokenwise_linear(const int8_t* a, const float* a_scale, const uint8_t* w, const float* w_scale,
+                            const void* bias, int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                            int W, int variant, void* stream);
+
 /* Debug export of the exact per-group int32 dots: dots[m, n, g] =
  * sum_{k in group g} a[m,k]*w[n,k], int32 [M, N, K/64].  These are the integer
  * accumulators of grouped_native.cu:70-74 / grouped.py:89, computed by the same
