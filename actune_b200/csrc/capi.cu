@@ -298,8 +298,29 @@ int run_tokenwise(const int8_t* a, const float* a_scale, const uint8_t* w, const
   if (rc != ACTUNE_OK) return rc;
   if (M == 0 || N == 0) return ACTUNE_OK;
   if (!aligned(a, 16) || !aligned(w, 16)) return ACTUNE_ERR_MISALIGNED;
-  const int bn = pick_bn(variant, M, N, g_devices[dev].num_sms);
   CUtensorMap ta, tw;
+  if (variant == ACTUNE_VARIANT_AUTO && M <= 16 && K % 128 == 0 && (K * W / 8) % 128 == 0) {
+    // Decode sizes: the weight-streaming kernel in its tokenwise mode.
+    rc = encode_map_blocks(&ta, a, M, K, (int)M, kGemvStageK / 128);
+    if (rc != ACTUNE_OK) return rc;
+    rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, kGemvStageK * W / 8 / 128);
+    if (rc != ACTUNE_OK) return rc;
+    GemmParams p{};
+    p.act_scale = a_scale;
+    p.w_scale = w_scale;
+    p.bias = bias;
+    p.out = out;
+    p.dots = nullptr;
+    p.M = (int)M;
+    p.N = (int)N;
+    p.K = (int)K;
+    p.G = (int)(K / 64);
+    p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
+    p.out_dtype = out_dtype;
+    p.out_vec_ok = 0;
+    return cuda_status(launch_gemv_tokenwise(W, ta, tw, p, g_devices[dev].num_sms, stream));
+  }
+  const int bn = pick_bn(variant, M, N, g_devices[dev].num_sms);
   rc = encode_map(&ta, a, M, K, 128, 128, Swz::B128);
   if (rc != ACTUNE_OK) return rc;
   rc = encode_map(&tw, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn, W == 8 ? Swz::B128 : Swz::None);

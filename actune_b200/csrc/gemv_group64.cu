@@ -339,7 +339,10 @@ struct Gemv4Cfg {
 
 enum : int { kGv4SiteFull = 61, kGv4SiteEmpty, kGv4SiteDotFull, kGv4SiteDotEmpty, kGv4SiteDrain };
 
-template <int W, int A, bool HI, bool DOTS>
+// TW (tokenwise backends): no per-group scales; the dot buffers carry the raw int32
+// dots, the chain warps add them exactly and apply float(acc) * as[m] * ws (+ bias)
+// once per row block (as: one scale per token).
+template <int W, int A, bool HI, bool DOTS, bool TW = false>
 __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
     gemv4_group64_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
                          const __grid_constant__ CUtensorMap tm_scale, const GemmParams p) {
@@ -380,7 +383,7 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
     // one instruction.
     if (lane < 3) {
       prefetch_tensormap(lane == 0 ? &tm_wgt : lane == 1 ? &tm_act : &tm_scale);
-      const uint32_t stage_tx = C::W_BYTES + Mb * (C::A_BLK * 128 + (DOTS ? 0 : C::GPS * 4));
+      const uint32_t stage_tx = C::W_BYTES + Mb * (C::A_BLK * 128 + ((DOTS || TW) ? 0 : C::GPS * 4));
       int issued = 0;
       for (int it = 0; it < total; ++it) {
         const int s = it % C::STAGES;
@@ -394,7 +397,7 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
         uint8_t* base = smem + s * C::STAGE_BYTES;
         if (lane == 0) tma_load_3d(base, &tm_wgt, 0, rb * C::ROWS, st * C::W_BLK, &full_bar[s]);
         else if (lane == 1) tma_load_3d(base + C::W_BYTES, &tm_act, 0, 0, st * C::A_BLK, &full_bar[s]);
-        else if (!DOTS) tma_load_2d(base + C::W_BYTES + C::A_BYTES, &tm_scale, st * C::GPS, 0, &full_bar[s]);
+        else if (!DOTS && !TW) tma_load_2d(base + C::W_BYTES + C::A_BYTES, &tm_scale, st * C::GPS, 0, &full_bar[s]);
         ++issued;
       }
       // Never leave the CTA with bulk copies still landing in shared memory.
@@ -424,7 +427,7 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
       const int rb = (int)blockIdx.x + (it / n_stages) * (int)gridDim.x, st = it % n_stages;
       const uint8_t* w_tile = smem + s * C::STAGE_BYTES;
       const uint8_t* a_tile = w_tile + C::W_BYTES;
-      if constexpr (!DOTS) {
+      if constexpr (!DOTS && !TW) {
         // K-lane 0 copies the stage's scales for its row group's chain warps, so that
         // the stage slot is free once the dots are written.
         if (q == 0) {
@@ -455,6 +458,14 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
               const int n = rb * C::ROWS + blk8 * 8 + 2 * t + (i & 1);
               if (m < p.M && n < p.N && g < G) p.dots[((int64_t)m * p.N + n) * G + g] = dd[i] >> C::SHIFT;
             }
+          } else if constexpr (TW) {
+            // Raw int32 dots (bit patterns in the float slots).
+            DotT* dst = dots_smem + ((d * 4 + blk8) * C::GPS + q * C::GPQ + j) * 32 + lane;
+            if constexpr (HI)
+              *dst = make_float4(__int_as_float(dd[0]), __int_as_float(dd[1]), __int_as_float(dd[2]),
+                                 __int_as_float(dd[3]));
+            else
+              *dst = make_float2(__int_as_float(dd[0]), __int_as_float(dd[1]));
           } else {
             DotT* dst = dots_smem + ((d * 4 + blk8) * C::GPS + q * C::GPQ + j) * 32 + lane;
             if constexpr (HI)
@@ -478,6 +489,10 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
     const bool has_bias = p.bias_dtype != kDtNone;
     const float shift_scale = 1.0f / float(1 << C::SHIFT);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int32_t iacc[4] = {0, 0, 0, 0};
+    // Tokenwise: one activation scale per token.
+    const float as0 = (TW && tok0) ? __ldg(p.act_scale + gid) : 0.f;
+    const float as1 = (TW && tok1) ? __ldg(p.act_scale + gid + 8) : 0.f;
     float ws_pre[2] = {0.f, 0.f}, bias_pre[2] = {0.f, 0.f};
     for (int it = 0; it < total; ++it) {
       const int d = it % C::DSTAGES;
@@ -491,8 +506,39 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
           bias_pre[i2] = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
         }
         acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        iacc[0] = iacc[1] = iacc[2] = iacc[3] = 0;
       }
       if (!mbar_wait(&dot_full[d][r], (it / C::DSTAGES) & 1, kGv4SiteDotFull)) break;
+      if constexpr (TW) {
+        const DotT* dslot = dots_smem + ((d * 4 + blk8) * C::GPS) * 32 + lane;
+#pragma unroll
+        for (int g = 0; g < C::GPS; ++g) {
+          const DotT dv = dslot[g * 32];
+          iacc[0] += __float_as_int(dv.x);
+          iacc[1] += __float_as_int(dv.y);
+          if constexpr (HI) {
+            iacc[2] += __float_as_int(dv.z);
+            iacc[3] += __float_as_int(dv.w);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dot_empty[d][r]);
+        if (st == n_stages - 1) {
+          // float(acc) exactly rounded; the 2^-SHIFT of top-bit codes is exact.
+          const float t00 = __int2float_rn(iacc[0]) * shift_scale * as0, t01 = __int2float_rn(iacc[1]) * shift_scale * as0;
+          const float t10 = __int2float_rn(iacc[2]) * shift_scale * as1, t11 = __int2float_rn(iacc[3]) * shift_scale * as1;
+#pragma unroll
+          for (int i2 = 0; i2 < 2; ++i2) {
+            const int n = rb * C::ROWS + blk8 * 8 + 2 * t + i2;
+            if (n >= p.N) continue;
+            const float ws = ws_pre[i2], bias = bias_pre[i2];
+            const float a0v = i2 ? t01 : t00, a1v = i2 ? t11 : t10;
+            if (tok0) store_scalar(p, (int64_t)gid * p.N + n, has_bias ? fmaf(a0v, ws, bias) : a0v * ws);
+            if (tok1) store_scalar(p, (int64_t)(gid + 8) * p.N + n, has_bias ? fmaf(a1v, ws, bias) : a1v * ws);
+          }
+        }
+        continue;
+      }
       const float* sc = dsc_smem + (d * 2 + r) * (C::TOK * C::GPS);
       const DotT* dslot = dots_smem + ((d * 4 + blk8) * C::GPS) * 32 + lane;
       // Groups past the end of K have dot 0 and scale 0 (zero fill): acc += 0 * 0.
@@ -525,12 +571,13 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
   }
 }
 
-template <int W, int A, bool HI>
+template <int W, int A, bool HI, bool TW = false>
 static cudaError_t launch_gemv4_hi(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
                                    const GemmParams& p, int num_sms, cudaStream_t stream) {
   using C = Gemv4Cfg<W, A, HI>;
-  const bool dots = p.dots != nullptr;
-  auto kernel = dots ? gemv4_group64_kernel<W, A, HI, true> : gemv4_group64_kernel<W, A, HI, false>;
+  const bool dots = !TW && p.dots != nullptr;
+  auto kernel = TW ? gemv4_group64_kernel<W, A, HI, false, TW>
+                   : (dots ? gemv4_group64_kernel<W, A, HI, true> : gemv4_group64_kernel<W, A, HI, false>);
   int dev = 0;
   cudaGetDevice(&dev);
   static bool configured[2][64] = {};
@@ -583,6 +630,18 @@ cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUten
   ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
   ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
   ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
+#undef ACTUNE_CASE
+  return cudaErrorInvalidValue;
+}
+
+// Tokenwise decode (M <= 16, 8-bit activations): the same kernel in its TW mode.
+cudaError_t launch_gemv_tokenwise(int W, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
+                                  int num_sms, cudaStream_t stream) {
+#define ACTUNE_CASE(WW)                                                                  \
+  if (W == WW)                                                                           \
+    return p.M > 8 ? launch_gemv4_hi<WW, 8, true, true>(ta, tw, ta, p, num_sms, stream)  \
+                   : launch_gemv4_hi<WW, 8, false, true>(ta, tw, ta, p, num_sms, stream);
+  ACTUNE_CASE(2) ACTUNE_CASE(4) ACTUNE_CASE(8)
 #undef ACTUNE_CASE
   return cudaErrorInvalidValue;
 }

@@ -22,6 +22,10 @@ cudaError_t launch_r4_refine(const void* w, int dtype, int64_t N, int64_t K, con
 // Without: 2-D maps with 128-byte-wide boxes of 16 * ceil(M / 16) token rows and 32
 // weight rows.  Packed boxes use the 128-byte swizzle.
 constexpr int kGemvStageK = 1024;
+// Tokenwise decode (M <= 16, K*W/8 and K multiples of 128 bytes): whole-stage maps as
+// above, no scale map; p.act_scale holds one scale per token.
+cudaError_t launch_gemv_tokenwise(int W, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
+                                  int num_sms, cudaStream_t stream);
 constexpr int kGemvRows = 32;
 cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap* ts,
                                 const GemmParams& p, int num_sms, cudaStream_t stream);

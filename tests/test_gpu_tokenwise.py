@@ -160,3 +160,23 @@ def test_tokenwise_rejects_bad_arguments(ops):
     ws = torch.ones(8, device=DEV)
     with pytest.raises(_lib.ActuneError):
         ops.tokenwise_linear(a, s, w, ws, None, 96, 4)  # K % 64 != 0
+
+
+@pytest.mark.parametrize("w", [4, 8, 2])
+@pytest.mark.parametrize("m", [1, 4, 9, 16])
+def test_tokenwise_decode_sizes(ops, w, m):
+    """M <= 16 runs the weight-streaming kernel in its tokenwise mode: fp32 outputs
+    bit-exact against the oracle, with and without bias, ragged N and a partial
+    last K stage (K = 1536)."""
+    torch.manual_seed(w * 100 + m)
+    for k, n, with_bias in ((4096, 4096, True), (1536, 200, False)):
+        x = torch.randn(m, k, device=DEV, dtype=torch.bfloat16)
+        lo, hi = {4: (-8, 8), 8: (-128, 128), 2: (-2, 2)}[w]
+        codes = torch.randint(lo, hi, (n, k), device=DEV, dtype=torch.int8)
+        ws = torch.rand(n, device=DEV) * 0.01
+        bias = (torch.randn(n, device=DEV) * 0.1).bfloat16() if with_bias else None
+        act, scale = ops.quantize_rows_a8(x)
+        y = ops.tokenwise_linear(act, scale, ops.pack_rows(codes, w), ws, bias, k, w, out_dtype=torch.float32)
+        ref = O.tokenwise_linear(act.cpu().numpy(), scale.cpu().numpy(), codes.cpu().numpy(), ws.cpu().numpy(),
+                                 None if bias is None else bias.float().cpu().numpy(), fma=True)
+        assert bits_equal(y.cpu().numpy(), ref), (k, n)
