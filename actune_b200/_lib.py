@@ -35,6 +35,8 @@ EXPORTS = (
     "actune_packed_linear",
     "actune_quantize_rows_a8",
     "actune_tokenwise_linear",
+    "actune_quantize_rows_a4",
+    "actune_rowwise_linear",
     "actune_packed_linear_dots",
     "actune_weight_codes",
     "actune_r4_refine",
@@ -66,6 +68,8 @@ def _declare(L):
     L.actune_packed_linear_dots.argtypes = [p, p, p, i64, i64, i64, i32, i32, i32, p]
     L.actune_quantize_rows_a8.argtypes = [p, i32, i64, i64, p, p, p]
     L.actune_tokenwise_linear.argtypes = [p, p, p, p, p, i32, p, i32, i64, i64, i64, i32, i32, p]
+    L.actune_quantize_rows_a4.argtypes = [p, i32, i64, i64, p, p, p]
+    L.actune_rowwise_linear.argtypes = [p, i32, p, p, i32, p, p, i32, p, i32, i64, i64, i64, i32, i32, p]
     L.actune_weight_codes.argtypes = [p, i32, i64, i64, i32, i32, p, p, p, p]
     L.actune_r4_refine.argtypes = [p, i32, i64, i64, p, p, p, p, p]
     L.actune_pack_rows.argtypes = [p, i64, i64, i32, p, p]

@@ -290,41 +290,16 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   return cuda_status(e);
 }
 
-int run_tokenwise(const int8_t* a, const float* a_scale, const uint8_t* w, const float* w_scale, const void* bias,
-                  int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K, int W, int variant,
-                  cudaStream_t stream) {
+// Row-scaled linear (the tokenwise A8 and per-row A4 backends): full-K int32 dots,
+// one activation scale per token, `order` 0 = (acc*as)*ws, 1 = acc*(as*ws).
+int run_rowwise(const uint8_t* a, int A, const float* a_scale, const uint8_t* w, int W, const float* w_scale,
+                const void* bias, int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K, int order,
+                int variant, cudaStream_t stream) {
   int dev = 0;
   int rc = current_device(&dev);
   if (rc != ACTUNE_OK) return rc;
   if (M == 0 || N == 0) return ACTUNE_OK;
   if (!aligned(a, 16) || !aligned(w, 16)) return ACTUNE_ERR_MISALIGNED;
-  CUtensorMap ta, tw;
-  if (variant == ACTUNE_VARIANT_AUTO && M <= 16 && K % 128 == 0 && (K * W / 8) % 128 == 0) {
-    // Decode sizes: the weight-streaming kernel in its tokenwise mode.
-    rc = encode_map_blocks(&ta, a, M, K, (int)M, kGemvStageK / 128);
-    if (rc != ACTUNE_OK) return rc;
-    rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, kGemvStageK * W / 8 / 128);
-    if (rc != ACTUNE_OK) return rc;
-    GemmParams p{};
-    p.act_scale = a_scale;
-    p.w_scale = w_scale;
-    p.bias = bias;
-    p.out = out;
-    p.dots = nullptr;
-    p.M = (int)M;
-    p.N = (int)N;
-    p.K = (int)K;
-    p.G = (int)(K / 64);
-    p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
-    p.out_dtype = out_dtype;
-    p.out_vec_ok = 0;
-    return cuda_status(launch_gemv_tokenwise(W, ta, tw, p, g_devices[dev].num_sms, stream));
-  }
-  const int bn = pick_bn(variant, M, N, g_devices[dev].num_sms);
-  rc = encode_map(&ta, a, M, K, 128, 128, Swz::B128);
-  if (rc != ACTUNE_OK) return rc;
-  rc = encode_map(&tw, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn, W == 8 ? Swz::B128 : Swz::None);
-  if (rc != ACTUNE_OK) return rc;
   GemmParams p{};
   p.act_scale = a_scale;
   p.w_scale = w_scale;
@@ -334,18 +309,35 @@ int run_tokenwise(const int8_t* a, const float* a_scale, const uint8_t* w, const
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
-  p.G = (int)((K + 63) / 64);  // stages of 128 codes; the zero fill past K adds nothing
   p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
   p.out_dtype = out_dtype;
+  p.rowwise_order = order;
+  CUtensorMap ta, tw;
+  if (variant == ACTUNE_VARIANT_AUTO && M <= 16 && (K * A / 8) % 128 == 0 && (K * W / 8) % 128 == 0) {
+    // Decode sizes: the weight-streaming kernel in its row-scaled mode.
+    rc = encode_map_blocks(&ta, a, M, K * A / 8, (int)M, kGemvStageK * A / 8 / 128);
+    if (rc != ACTUNE_OK) return rc;
+    rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, kGemvStageK * W / 8 / 128);
+    if (rc != ACTUNE_OK) return rc;
+    p.G = (int)(K / 64);
+    p.out_vec_ok = 0;
+    return cuda_status(launch_gemv_tokenwise(W, A, ta, tw, p, g_devices[dev].num_sms, stream));
+  }
+  const int bn = pick_bn(variant, M, N, g_devices[dev].num_sms);
+  rc = encode_map(&ta, a, M, K * A / 8, A == 8 ? 128 : 16 * A, 128, A == 8 ? Swz::B128 : Swz::None);
+  if (rc != ACTUNE_OK) return rc;
+  rc = encode_map(&tw, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn, W == 8 ? Swz::B128 : Swz::None);
+  if (rc != ACTUNE_OK) return rc;
+  p.G = (int)((K + 63) / 64);  // stages of 128 codes; the zero fill past K adds nothing
   p.out_vec_ok = (N % 8 == 0) && aligned(out, 16);
   cudaError_t e = cudaErrorInvalidValue;
-#define ACTUNE_TW(WW)                                                              \
-  if (W == WW) {                                                                   \
-    e = bn == 32   ? launch_group64_tokenwise<WW, 32>(ta, tw, p, stream)           \
-        : bn == 64 ? launch_group64_tokenwise<WW, 64>(ta, tw, p, stream)           \
-                   : launch_group64_tokenwise<WW, 128>(ta, tw, p, stream);         \
+#define ACTUNE_TW(WW, AA)                                                              \
+  if (W == WW && A == AA) {                                                            \
+    e = bn == 32   ? launch_group64_tokenwise<WW, AA, 32>(ta, tw, p, stream)           \
+        : bn == 64 ? launch_group64_tokenwise<WW, AA, 64>(ta, tw, p, stream)           \
+                   : launch_group64_tokenwise<WW, AA, 128>(ta, tw, p, stream);         \
   }
-  ACTUNE_TW(2) ACTUNE_TW(4) ACTUNE_TW(8)
+  ACTUNE_TW(2, 8) ACTUNE_TW(4, 8) ACTUNE_TW(8, 8) ACTUNE_TW(2, 4) ACTUNE_TW(4, 4) ACTUNE_TW(8, 4)
 #undef ACTUNE_TW
   return cuda_status(e);
 }
@@ -418,7 +410,21 @@ int actune_quantize_rows_a8(const void* x, int x_dtype, int64_t M, int64_t K, in
   if (M == 0) return ACTUNE_OK;
   if (!aligned(x, 16) || !aligned(codes, 8) || !aligned(scales, 4)) return ACTUNE_ERR_MISALIGNED;
   const int dt = x_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (x_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
-  return cuda_status(launch_quantize_rows_a8(x, dt, M, K, codes, scales, reinterpret_cast<cudaStream_t>(stream)));
+  return cuda_status(launch_quantize_rows(x, dt, M, K, 8, reinterpret_cast<uint8_t*>(codes), scales,
+                                          reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int actune_quantize_rows_a4(const void* x, int x_dtype, int64_t M, int64_t K, uint8_t* packed, float* scales,
+                            void* stream) {
+  if (!valid_float_dtype(x_dtype) || M < 0 || K <= 0 || K % 8) return ACTUNE_ERR_INVALID_VALUE;
+  if (M > 0 && (x == nullptr || packed == nullptr || scales == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != ACTUNE_OK) return rc;
+  if (M == 0) return ACTUNE_OK;
+  if (!aligned(x, 16) || !aligned(packed, 4) || !aligned(scales, 4)) return ACTUNE_ERR_MISALIGNED;
+  const int dt = x_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (x_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
+  return cuda_status(launch_quantize_rows(x, dt, M, K, 4, packed, scales, reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int actune_tokenwise_linear(const int8_t* a, const float* a_scale, const uint8_t* w, const float* w_scale,
@@ -438,8 +444,29 @@ int actune_tokenwise_linear(const int8_t* a, const float* a_scale, const uint8_t
                                   : (bias_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16
                                                                      : (bias_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32));
   const int odt = out_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (out_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
-  return run_tokenwise(a, a_scale, w, w_scale, bias, bdt, out, odt, M, N, K, W, variant,
-                       reinterpret_cast<cudaStream_t>(stream));
+  return run_rowwise(reinterpret_cast<const uint8_t*>(a), 8, a_scale, w, W, w_scale, bias, bdt, out, odt, M, N, K, 0,
+                     variant, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int actune_rowwise_linear(const uint8_t* a, int A, const float* a_scale, const uint8_t* w, int W, const float* w_scale,
+                          const void* bias, int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                          int order, int variant, void* stream) {
+  if (!valid_bits(W) || (A != 4 && A != 8) || (order != 0 && order != 1) || K <= 0 || K % 64 ||
+      K > (int64_t(1) << 24) || M < 0 || N < 0 || M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31))
+    return ACTUNE_ERR_INVALID_VALUE;
+  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_BN128) return ACTUNE_ERR_INVALID_VALUE;
+  if (bias != nullptr && !valid_float_dtype(bias_dtype)) return ACTUNE_ERR_INVALID_VALUE;
+  if (M > 0 && N > 0 && (a == nullptr || a_scale == nullptr || w == nullptr || w_scale == nullptr || out == nullptr))
+    return ACTUNE_ERR_INVALID_VALUE;
+  if (!aligned(a_scale, 4) || !aligned(w_scale, 4) || !aligned(out, dtype_size(out_dtype)) ||
+      (bias != nullptr && !aligned(bias, dtype_size(bias_dtype))))
+    return ACTUNE_ERR_MISALIGNED;
+  const int bdt = bias == nullptr ? kDtNone
+                                  : (bias_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16
+                                                                     : (bias_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32));
+  const int odt = out_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (out_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
+  return run_rowwise(a, A, a_scale, w, W, w_scale, bias, bdt, out, odt, M, N, K, order, variant,
+                     reinterpret_cast<cudaStream_t>(stream));
 }
 
 int actune_packed_linear_dots(const uint8_t* a, const uint8_t* w, int32_t* dots, int64_t M, int64_t N, int64_t K,

@@ -40,6 +40,7 @@ struct GemmParams {
   int bias_dtype;
   int out_dtype;
   int out_vec_ok;          // N % 8 == 0 and out 16-byte aligned
+  int rowwise_order;       // row-scaled modes: 0 (acc*as)*ws, 1 acc*(as*ws) (the per-row A4 native order)
 };
 
 // Wait-site identifiers recorded with a device timeout.
@@ -131,6 +132,14 @@ __device__ __forceinline__ float finish(float acc, const GemmParams& p, int n) {
   const float ws = __ldg(p.w_scale + n);
   if (p.bias_dtype != kDtNone) return fmaf(acc, ws, load_bias(p.bias, p.bias_dtype, n));
   return acc * ws;
+}
+
+// Row-scaled epilogue in the per-row A4 native order (native_s4_extension_kernel.cu:
+// 229-233): y = acc * (as[m] * ws[n]) (+ bias, fused).
+__device__ __forceinline__ float finish_native(float acc, const GemmParams& p, int n, float as_m) {
+  const float s = as_m * __ldg(p.w_scale + n);
+  if (p.bias_dtype != kDtNone) return fmaf(acc, s, load_bias(p.bias, p.bias_dtype, n));
+  return acc * s;
 }
 
 __device__ __forceinline__ void store_scalar(const GemmParams& p, int64_t idx, float y) {
@@ -412,7 +421,8 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
       ok = mbar_wait(&acc_full[0], 0, kSiteEpilogue);
       if (ok) {
         tc_fence_after();
-        const float as_m = (m < p.M) ? __ldg(p.act_scale + m) : 0.f;
+        // Order 1 applies as[m] with ws in the final store.
+        const float as_m = p.rowwise_order ? 1.f : ((m < p.M) ? __ldg(p.act_scale + m) : 0.f);
 #pragma unroll
         for (int part = 0; part < C::COLS / H; ++part) {
           tmem_ld<H>(lane_base + part * H, ra);
@@ -525,10 +535,13 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
           const float4 hi = *reinterpret_cast<const float4*>(stage_buf + r * LD + c8 + 4);
           const float a8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
           const int64_t orow = (int64_t)(m0 + r) * p.N;
+          const bool native = TW && p.rowwise_order;
+          const float as_r = native ? __ldg(p.act_scale + m0 + r) : 0.f;
+          auto fin = [&](float a, int nn) { return native ? finish_native(a, p, nn, as_r) : finish(a, p, nn); };
           if (p.out_vec_ok && n + 8 <= p.N && p.out_dtype != kDtF32) {
             float y[8];
 #pragma unroll
-            for (int t = 0; t < 8; ++t) y[t] = finish(a8[t], p, n + t);
+            for (int t = 0; t < 8; ++t) y[t] = fin(a8[t], n + t);
             uint4 v;
             if (p.out_dtype == kDtBF16) {
               __nv_bfloat162 h0 = __floats2bfloat162_rn(y[0], y[1]), h1 = __floats2bfloat162_rn(y[2], y[3]);
@@ -545,7 +558,7 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
           } else {
 #pragma unroll
             for (int t = 0; t < 8; ++t)
-              if (n + t < p.N) store_scalar(p, orow + n + t, finish(a8[t], p, n + t));
+              if (n + t < p.N) store_scalar(p, orow + n + t, fin(a8[t], n + t));
           }
         }
       }
@@ -564,8 +577,8 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
 template <int W, int A, int BN>
 cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
                                 cudaStream_t stream);
-// Tokenwise mode (A = 8 codes, per-token act_scale [M]).
-template <int W, int BN>
+// Row-scaled mode (per-token act_scale [M]; A = 8 tokenwise, A = 4 per-row A4).
+template <int W, int A, int BN>
 cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
                                      cudaStream_t stream);
 

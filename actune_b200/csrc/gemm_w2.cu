@@ -23,11 +23,11 @@ cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm
   return cudaGetLastError();
 }
 
-template <int W, int BN>
+template <int W, int A, int BN>
 cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
                                      cudaStream_t stream) {
-  using C = Group64Cfg<W, 8, BN>;
-  auto kernel = group64_gemm_kernel<W, 8, BN, false, true>;
+  using C = Group64Cfg<W, A, BN>;
+  auto kernel = group64_gemm_kernel<W, A, BN, false, true>;
   int dev = 0;
   cudaGetDevice(&dev);
   static bool configured[64] = {};
@@ -42,9 +42,12 @@ cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMa
   return cudaGetLastError();
 }
 
-template cudaError_t launch_group64_tokenwise<2, 32>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-template cudaError_t launch_group64_tokenwise<2, 64>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-template cudaError_t launch_group64_tokenwise<2, 128>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+template cudaError_t launch_group64_tokenwise<2, 4, 32>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+template cudaError_t launch_group64_tokenwise<2, 4, 64>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+template cudaError_t launch_group64_tokenwise<2, 4, 128>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+template cudaError_t launch_group64_tokenwise<2, 8, 32>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+template cudaError_t launch_group64_tokenwise<2, 8, 64>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+template cudaError_t launch_group64_tokenwise<2, 8, 128>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
 
 #define ACTUNE_INST(A, BN)                                                                                  \
   template cudaError_t launch_group64_gemm<2, A, BN>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, \

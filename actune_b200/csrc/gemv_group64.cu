@@ -524,17 +524,21 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&dot_empty[d][r]);
         if (st == n_stages - 1) {
-          // float(acc) exactly rounded; the 2^-SHIFT of top-bit codes is exact.
-          const float t00 = __int2float_rn(iacc[0]) * shift_scale * as0, t01 = __int2float_rn(iacc[1]) * shift_scale * as0;
-          const float t10 = __int2float_rn(iacc[2]) * shift_scale * as1, t11 = __int2float_rn(iacc[3]) * shift_scale * as1;
+          // float(acc) exactly rounded; the 2^-SHIFT of top-bit codes is exact.  Order 0:
+          // y = (f * as) * ws (+ bias, fused); order 1: y = f * (as * ws) (+ bias, fused).
+          const float f00 = __int2float_rn(iacc[0]) * shift_scale, f01 = __int2float_rn(iacc[1]) * shift_scale;
+          const float f10 = __int2float_rn(iacc[2]) * shift_scale, f11 = __int2float_rn(iacc[3]) * shift_scale;
+          const bool native = p.rowwise_order != 0;
 #pragma unroll
           for (int i2 = 0; i2 < 2; ++i2) {
             const int n = rb * C::ROWS + blk8 * 8 + 2 * t + i2;
             if (n >= p.N) continue;
             const float ws = ws_pre[i2], bias = bias_pre[i2];
-            const float a0v = i2 ? t01 : t00, a1v = i2 ? t11 : t10;
-            if (tok0) store_scalar(p, (int64_t)gid * p.N + n, has_bias ? fmaf(a0v, ws, bias) : a0v * ws);
-            if (tok1) store_scalar(p, (int64_t)(gid + 8) * p.N + n, has_bias ? fmaf(a1v, ws, bias) : a1v * ws);
+            const float f0 = i2 ? f01 : f00, f1 = i2 ? f11 : f10;
+            const float m0 = native ? f0 : f0 * as0, s0 = native ? as0 * ws : ws;
+            const float m1 = native ? f1 : f1 * as1, s1 = native ? as1 * ws : ws;
+            if (tok0) store_scalar(p, (int64_t)gid * p.N + n, has_bias ? fmaf(m0, s0, bias) : m0 * s0);
+            if (tok1) store_scalar(p, (int64_t)(gid + 8) * p.N + n, has_bias ? fmaf(m1, s1, bias) : m1 * s1);
           }
         }
         continue;
@@ -634,14 +638,16 @@ cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUten
   return cudaErrorInvalidValue;
 }
 
-// Tokenwise decode (M <= 16, 8-bit activations): the same kernel in its TW mode.
-cudaError_t launch_gemv_tokenwise(int W, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
+// Row-scaled decode (M <= 16; A = 8 tokenwise, A = 4 per-row A4): the same kernel in
+// its TW mode.
+cudaError_t launch_gemv_tokenwise(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
                                   int num_sms, cudaStream_t stream) {
-#define ACTUNE_CASE(WW)                                                                  \
-  if (W == WW)                                                                           \
-    return p.M > 8 ? launch_gemv4_hi<WW, 8, true, true>(ta, tw, ta, p, num_sms, stream)  \
-                   : launch_gemv4_hi<WW, 8, false, true>(ta, tw, ta, p, num_sms, stream);
-  ACTUNE_CASE(2) ACTUNE_CASE(4) ACTUNE_CASE(8)
+#define ACTUNE_CASE(WW, AA)                                                                \
+  if (W == WW && A == AA)                                                                  \
+    return p.M > 8 ? launch_gemv4_hi<WW, AA, true, true>(ta, tw, ta, p, num_sms, stream)   \
+                   : launch_gemv4_hi<WW, AA, false, true>(ta, tw, ta, p, num_sms, stream);
+  ACTUNE_CASE(2, 8) ACTUNE_CASE(4, 8) ACTUNE_CASE(8, 8)
+  ACTUNE_CASE(2, 4) ACTUNE_CASE(4, 4) ACTUNE_CASE(8, 4)
 #undef ACTUNE_CASE
   return cudaErrorInvalidValue;
 }

@@ -6,9 +6,10 @@
 
 namespace actune {
 
-// Per-row dynamic INT8 quantizer of the tokenwise backends (K % 8 == 0, 16-byte aligned x).
-cudaError_t launch_quantize_rows_a8(const void* x, int dtype, int64_t M, int64_t K, int8_t* codes, float* scales,
-                                    cudaStream_t stream);
+// Per-row dynamic quantizer of the tokenwise (bits 8: int8 codes [M, K]) and per-row
+// A4 (bits 4: packed [M, K/2]) backends (K % 8 == 0, 16-byte aligned x).
+cudaError_t launch_quantize_rows(const void* x, int dtype, int64_t M, int64_t K, int bits, uint8_t* codes,
+                                 float* scales, cudaStream_t stream);
 cudaError_t launch_quantize_group64(const void* x, int dtype, int64_t groups, int A, uint8_t* packed, float* scales,
                                     int num_sms, cudaStream_t stream);
 cudaError_t launch_weight_codes(const void* w, int dtype, int64_t N, int64_t K, int W, int A, const float* clip,
@@ -24,7 +25,7 @@ cudaError_t launch_r4_refine(const void* w, int dtype, int64_t N, int64_t K, con
 constexpr int kGemvStageK = 1024;
 // Tokenwise decode (M <= 16, K*W/8 and K multiples of 128 bytes): whole-stage maps as
 // above, no scale map; p.act_scale holds one scale per token.
-cudaError_t launch_gemv_tokenwise(int W, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
+cudaError_t launch_gemv_tokenwise(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
                                   int num_sms, cudaStream_t stream);
 constexpr int kGemvRows = 32;
 cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap* ts,

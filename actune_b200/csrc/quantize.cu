@@ -228,16 +228,22 @@ cudaError_t launch_quantize_group64(const void* x, int dtype, int64_t groups, in
   }
 }
 
-// Per-row dynamic INT8 activation quantizer of the tokenwise backends, restating
-// actune/kernels/w4a8_triton.py:161-201: scale = max(row absmax, 1e-8) * fp32(1/127)
-// (a multiply by the binary32 reciprocal, which is what torch computes for a CUDA
-// tensor divided by a scalar and what the reference reproduces on purpose), then
-// code = clamp(rint(x / scale), -128, 127) with IEEE division.  One CTA per row;
-// each thread holds up to CPT chunks of 8 values in registers between the absmax
-// and the quantizing pass (CPT == 0: K beyond the register cache, read twice).
-template <typename T, int CPT>
-__global__ void __launch_bounds__(256) quantize_rows_a8_kernel(const T* __restrict__ x, int8_t* __restrict__ codes,
-                                                               float* __restrict__ scales, int64_t K) {
+// Per-row dynamic activation quantizers of the tokenwise (A8) and per-row A4
+// backends, restating actune/kernels/w4a8_triton.py:161-201 (BITS 8) and
+// actune/kernels/wxa4_native.py:27-64 (BITS 4):
+//   scale = max(row absmax, 1e-8) * fp32(1/P),  P = 2^(BITS-1) - 1
+//   (a multiply by the binary32 reciprocal, which is what torch computes for a CUDA
+//   tensor divided by a scalar and what the reference reproduces on purpose), then
+//   code = clamp(rint(x / scale), -P-1, P) with IEEE division.
+// BITS 8 stores int8 codes [M, K]; BITS 4 packs two codes per byte, even k in the
+// low nibble (the group-64 row layout).  One CTA per row; each thread holds up to
+// CPT chunks of 8 values in registers between the absmax and the quantizing pass
+// (CPT == 0: K beyond the register cache, read twice).
+template <typename T, int CPT, int BITS>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ x, uint8_t* __restrict__ codes,
+                                                            float* __restrict__ scales, int64_t K) {
+  constexpr float kPos = float((1 << (BITS - 1)) - 1);
+  constexpr float kNeg = -float(1 << (BITS - 1));
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   const T* xr = x + row * K;
@@ -268,7 +274,7 @@ __global__ void __launch_bounds__(256) quantize_rows_a8_kernel(const T* __restri
   float a = red[0];
 #pragma unroll
   for (int w = 1; w < 8; ++w) a = fmaxf(a, red[w]);
-  const float recip = 1.0f / 127.0f;  // binary32 reciprocal, folded at compile time
+  const float recip = 1.0f / kPos;  // binary32 reciprocal, folded at compile time
   const float scale = fmaxf(a, 1e-8f) * recip;
   if (threadIdx.x == 0) scales[row] = scale;
   auto emit = [&](const float (&vv)[8], int64_t i) {
@@ -276,10 +282,16 @@ __global__ void __launch_bounds__(256) quantize_rows_a8_kernel(const T* __restri
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       float q = rintf(__fdiv_rn(vv[k], scale));
-      q = fminf(fmaxf(q, -128.f), 127.f);
-      word[k >> 2] |= ((uint32_t)((int)q) & 0xFFu) << ((k & 3) * 8);
+      q = fminf(fmaxf(q, kNeg), kPos);
+      const uint32_t field = (uint32_t)((int)q) & ((1u << BITS) - 1);
+      const int bit = k * BITS;
+      word[bit >> 5] |= field << (bit & 31);
     }
-    *reinterpret_cast<uint2*>(codes + row * K + i) = make_uint2(word[0], word[1]);
+    if constexpr (BITS == 8) {
+      *reinterpret_cast<uint2*>(codes + row * K + i) = make_uint2(word[0], word[1]);
+    } else {
+      *reinterpret_cast<uint32_t*>(codes + (row * K + i) / 2) = word[0];
+    }
   };
   if constexpr (CPT > 0) {
 #pragma unroll
@@ -295,24 +307,31 @@ __global__ void __launch_bounds__(256) quantize_rows_a8_kernel(const T* __restri
   }
 }
 
-template <typename T>
-static cudaError_t launch_rows_t(const T* x, int64_t M, int64_t K, int8_t* codes, float* scales, cudaStream_t s) {
+template <typename T, int BITS>
+static cudaError_t launch_rows_t(const T* x, int64_t M, int64_t K, uint8_t* codes, float* scales, cudaStream_t s) {
   const unsigned grid = (unsigned)M;
-  if (K <= 2048) quantize_rows_a8_kernel<T, 1><<<grid, 256, 0, s>>>(x, codes, scales, K);
-  else if (K <= 4096) quantize_rows_a8_kernel<T, 2><<<grid, 256, 0, s>>>(x, codes, scales, K);
-  else if (K <= 8192) quantize_rows_a8_kernel<T, 4><<<grid, 256, 0, s>>>(x, codes, scales, K);
-  else quantize_rows_a8_kernel<T, 0><<<grid, 256, 0, s>>>(x, codes, scales, K);
+  if (K <= 2048) quantize_rows_kernel<T, 1, BITS><<<grid, 256, 0, s>>>(x, codes, scales, K);
+  else if (K <= 4096) quantize_rows_kernel<T, 2, BITS><<<grid, 256, 0, s>>>(x, codes, scales, K);
+  else if (K <= 8192) quantize_rows_kernel<T, 4, BITS><<<grid, 256, 0, s>>>(x, codes, scales, K);
+  else quantize_rows_kernel<T, 0, BITS><<<grid, 256, 0, s>>>(x, codes, scales, K);
   return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_rows_a8(const void* x, int dtype, int64_t M, int64_t K, int8_t* codes, float* scales,
+template <int BITS>
+static cudaError_t launch_rows_bits(const void* x, int dtype, int64_t M, int64_t K, uint8_t* codes, float* scales,
                                     cudaStream_t stream) {
-  if (M == 0) return cudaSuccess;
   switch (dtype) {
-    case kDtBF16: return launch_rows_t(reinterpret_cast<const __nv_bfloat16*>(x), M, K, codes, scales, stream);
-    case kDtF16: return launch_rows_t(reinterpret_cast<const __half*>(x), M, K, codes, scales, stream);
-    default: return launch_rows_t(reinterpret_cast<const float*>(x), M, K, codes, scales, stream);
+    case kDtBF16: return launch_rows_t<__nv_bfloat16, BITS>(reinterpret_cast<const __nv_bfloat16*>(x), M, K, codes, scales, stream);
+    case kDtF16: return launch_rows_t<__half, BITS>(reinterpret_cast<const __half*>(x), M, K, codes, scales, stream);
+    default: return launch_rows_t<float, BITS>(reinterpret_cast<const float*>(x), M, K, codes, scales, stream);
   }
+}
+
+cudaError_t launch_quantize_rows(const void* x, int dtype, int64_t M, int64_t K, int bits, uint8_t* codes,
+                                 float* scales, cudaStream_t stream) {
+  if (M == 0) return cudaSuccess;
+  return bits == 4 ? launch_rows_bits<4>(x, dtype, M, K, codes, scales, stream)
+                   : launch_rows_bits<8>(x, dtype, M, K, codes, scales, stream);
 }
 
 cudaError_t launch_weight_codes(const void* w, int dtype, int64_t N, int64_t K, int W, int A, const float* clip,

@@ -14,7 +14,8 @@ non-persistent buffer, the same codes packed as rows [N, K*W/8] for the kernel
 
 Sibling projections: ``shared_a8_cache_scope`` keeps the quantized activations of
 the most recent input so Q/K/V and gate/up reuse one quantization
-(w4a8_triton.py:204-325).
+(w4a8_triton.py:204-325); the per-row A4 backends keep theirs in the same scope's
+``a4_entry`` (wxa4_native.py:123-160).
 """
 from __future__ import annotations
 
@@ -95,6 +96,36 @@ def quantize_rows_shared(source: torch.Tensor, flat: torch.Tensor, *, in_feature
     state.misses += 1
     state.entry = _SharedA8Entry(source, in_features, activation, scale) if state.enabled else None
     return activation, scale
+
+
+class _SharedA4Entry:
+    """One task-local dynamic-A4 result (packed nibble rows and row scales)."""
+
+    __slots__ = ("source", "in_features", "packed", "scale")
+
+    def __init__(self, source, in_features, packed, scale):
+        self.source = source
+        self.in_features = in_features
+        self.packed = packed
+        self.scale = scale
+
+
+def quantize_rows_a4_shared(source: torch.Tensor, flat: torch.Tensor, *, in_features: int):
+    """Per-row INT4 activations of ``flat`` as packed nibble rows [M, K/2] and row
+    scales, reused by the next A4 projection reading the same ``source`` object
+    inside a ``shared_a8_cache_scope``; outside a scope nothing is cached
+    (wxa4_native.py:123-160)."""
+    if not source.is_cuda or flat.shape[-1] != in_features:
+        raise ValueError("native A4 quantization requires a CUDA input with matching K")
+    state = _SHARED_A8_STATE.get()
+    entry = None if state is None else state.a4_entry
+    if (entry is not None and entry.source is source and entry.in_features == in_features
+            and entry.packed.shape[0] == flat.shape[0]):
+        return entry.packed, entry.scale
+    packed, scale = ops.quantize_rows_a4(flat.contiguous())
+    if state is not None and state.enabled:
+        state.a4_entry = _SharedA4Entry(source, in_features, packed, scale)
+    return packed, scale
 
 
 class TokenwiseLinear(torch.nn.Module):

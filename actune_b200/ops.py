@@ -131,6 +131,53 @@ def tokenwise_linear(a, a_scale, w_rows, w_scale, bias, K: int, W: int, out_dtyp
     return out
 
 
+def quantize_rows_a4(x, packed=None, scales=None):
+    """Per-row dynamic INT4 activations of x [M, K]: (packed u8 [M, K/2] with even k in
+    the low nibble, scales f32 [M]), scale = max(row absmax, 1e-8) * fp32(1/7),
+    reference wxa4_native.py:27-64."""
+    _require(x.dim() == 2, "x must be 2-D [M, K]")
+    m, k = x.shape
+    _require(k % 8 == 0, "K must be a multiple of 8")
+    if packed is None:
+        packed = torch.empty((m, k // 2), device=x.device, dtype=torch.uint8)
+    if scales is None:
+        scales = torch.empty(m, device=x.device, dtype=torch.float32)
+    dev = _cuda_contig(x, packed, scales)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().actune_quantize_rows_a4(_ptr(x), dtype_code(x.dtype), m, k, _ptr(packed), _ptr(scales),
+                                                      _stream(dev)), "quantize_rows_a4")
+    return packed, scales
+
+
+ORDER_TRITON = 0   # (float(acc) * as) * ws (+ bias): the Triton tokenwise kernels
+ORDER_NATIVE = 1   # float(acc) * (as * ws) (+ bias): the native S4 CUDA kernels
+
+
+def rowwise_linear(a, A: int, a_scale, w_rows, W: int, w_scale, bias, K: int, order: int = ORDER_TRITON,
+                   out_dtype=torch.bfloat16, variant: int = _lib.VARIANT_AUTO, out: torch.Tensor | None = None):
+    """Row-scaled linear for A-bit activation rows [M, K*A/8] (A = 8 int8 codes, A = 4
+    packed nibbles) and W-bit weight rows [N, K*W/8]: exact int32 dots over all of K,
+    one scale per token and per output channel, epilogue in ``order``."""
+    _require(a.dim() == 2 and w_rows.dim() == 2, "rank mismatch")
+    _require(A in (4, 8) and W in (2, 4, 8), "Unsupported integer width")
+    m, n = a.shape[0], w_rows.shape[0]
+    _require(a.dtype in (torch.uint8, torch.int8) and w_rows.dtype == torch.uint8, "packed uint8 rows required")
+    _require(a.shape[1] == K * A // 8 and w_rows.shape[1] == K * W // 8, "packed shape mismatch")
+    _require(a_scale.numel() == m and w_scale.numel() == n, "scale shape mismatch")
+    _require(a_scale.dtype == torch.float32 and w_scale.dtype == torch.float32, "float scales required")
+    if bias is not None and bias.numel() == 0:
+        bias = None
+    if out is None:
+        out = torch.empty((m, n), device=a.device, dtype=out_dtype)
+    dev = _cuda_contig(a, a_scale, w_rows, w_scale, bias, out)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().actune_rowwise_linear(
+            _ptr(a), A, _ptr(a_scale), _ptr(w_rows), W, _ptr(w_scale), _ptr(bias),
+            _lib.DTYPE_NONE if bias is None else dtype_code(bias.dtype), _ptr(out), dtype_code(out.dtype),
+            m, n, K, int(order), int(variant), _stream(dev)), "rowwise_linear")
+    return out
+
+
 def packed_linear_dots(a, w, K: int, W: int, A: int, variant: int = _lib.VARIANT_AUTO):
     """Exact per-group int32 dots [M, N, K/64] from the tensor-core kernel (debug export)."""
     m, n = a.shape[0], w.shape[0]

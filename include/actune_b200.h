@@ -112,6 +112,25 @@ int actune_tokenwise_linear(const int8_t* a, const float* a_scale, const uint8_t
                             const void* bias, int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
                             int W, int variant, void* stream);
 
+/* Per-row A4 backends (replace actune/kernels/wxa4_native.py).
+ *
+ * actune_quantize_rows_a4: per-row dynamic signed INT4 activations of x [M, K]:
+ * scale[m] = max(row absmax, 1e-8) * fp32(1/7), codes = clamp(rint(x / scale), -8, 7),
+ * packed two per byte (even k in the low nibble) into packed [M, K/2]; replaces
+ * _quantize_rows_a4_kernel, wxa4_native.py:27-64.
+ *
+ * actune_rowwise_linear: actune_tokenwise_linear for A-bit activations packed as
+ * rows [M, K*A/8] (A = 8: int8; A = 4: actune_quantize_rows_a4 layout) and the
+ * epilogue order of the replaced kernel: order 0 = (float(acc) * as[m]) * ws[n]
+ * (+ bias), the Triton kernels (W8A4 runs _w8a8_gemm_kernel, wxa4_native.py:
+ * 370-389); order 1 = float(acc) * (as[m] * ws[n]) (+ bias), the native S4 CUDA
+ * kernels (native_s4_extension_kernel.cu:229-233).  K % 64 == 0. */
+int actune_quantize_rows_a4(const void* x, int x_dtype, int64_t M, int64_t K, uint8_t* packed, float* scales,
+                            void* stream);
+int actune_rowwise_linear(const uint8_t* a, int A, const float* a_scale, const uint8_t* w, int W, const float* w_scale,
+                          const void* bias, int bias_dtype, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                          int order, int variant, void* stream);
+
 /* Debug export of the exact per-group int32 dots: dots[m, n, g] =
  * sum_{k in group g} a[m,k]*w[n,k], int32 [M, N, K/64].  These are the integer
  * accumulators of grouped_native.cu:70-74 / grouped.py:89, computed by the same

@@ -339,4 +339,63 @@ int oracle_tokenwise_linear(const int8_t* a, const float* as, const int8_t* code
     return 0;
 }
 
+/* ---- per-row A4 backends (reference actune/kernels/wxa4_native.py) ---- */
+
+/* Per-row dynamic INT4 activations, _quantize_rows_a4_kernel (wxa4_native.py:27-64):
+ * scale = max(absmax, 1e-8) * fp32(1/7); codes clamp(rint(x / scale), -8, 7) with
+ * the division correctly rounded; two codes per byte, even k in the low nibble;
+ * packed is [M, (K+1)/2]. */
+int oracle_quantize_rows_a4(const uint16_t* x, int64_t M, int64_t K, uint8_t* packed, float* scales) {
+    if (M < 0 || K <= 0) return 1;
+    const float recip = 1.0f / 7.0f;
+    const int64_t KB = (K + 1) / 2;
+    for (int64_t m = 0; m < M; ++m) {
+        const uint16_t* row = x + m * K;
+        float amax = 0.0f;
+        for (int64_t k = 0; k < K; ++k) {
+            const float v = fabsf(bf16_to_f32(row[k]));
+            if (v > amax) amax = v;
+        }
+        const float scale = (amax > 1e-8f ? amax : 1e-8f) * recip;
+        scales[m] = scale;
+        for (int64_t j = 0; j < KB; ++j) {
+            int nib[2] = {0, 0};
+            for (int h = 0; h < 2; ++h) {
+                const int64_t k = 2 * j + h;
+                float q = k < K ? rintf(bf16_to_f32(row[k]) / scale) : 0.0f;
+                if (q < -8.0f) q = -8.0f;
+                if (q > 7.0f) q = 7.0f;
+                nib[h] = ((int)q) & 15;
+            }
+            packed[m * KB + j] = (uint8_t)(nib[0] | (nib[1] << 4));
+        }
+    }
+    return 0;
+}
+
+/* The native W{2,4}A4 epilogue (native_s4_extension_kernel.cu:226-234): exact int32
+ * dot over all of K, then value = float(acc); value *= as[m] * ws[n] (the scale
+ * product rounded first); value += bias[n] (fma_mode 1 fuses the multiply and add,
+ * as nvcc contracts them; 0 rounds twice).  a is [M, K] int8 codes, codes [N, K]. */
+int oracle_rowwise_native_linear(const int8_t* a, const float* as, const int8_t* codes, const float* ws,
+                                 const float* bias, int64_t M, int64_t N, int64_t K, int fma_mode, float* out) {
+    if (M < 0 || N < 0 || K <= 0) return 1;
+    for (int64_t m = 0; m < M; ++m) {
+        for (int64_t n = 0; n < N; ++n) {
+            int64_t acc = 0;
+            for (int64_t k = 0; k < K; ++k) acc += (int64_t)a[m * K + k] * (int64_t)codes[n * K + k];
+            const float f = (float)(int32_t)acc;
+            const float s = as[m] * ws[n];
+            float y;
+            if (bias) {
+                y = fma_mode ? fmaf(f, s, bias[n]) : f * s + bias[n];
+            } else {
+                y = f * s;
+            }
+            out[m * N + n] = y;
+        }
+    }
+    return 0;
+}
+
 int oracle_abi_version(void) { return 1; }

@@ -54,6 +54,8 @@ def lib():
         L.oracle_weight_codes.argtypes = [p, i64, i64, i32, i32, p, p, p]
         L.oracle_quantize_rows_a8.argtypes = [p, i64, i64, p, p]
         L.oracle_tokenwise_linear.argtypes = [p, p, p, p, p, i64, i64, i64, i32, p]
+        L.oracle_quantize_rows_a4.argtypes = [p, i64, i64, p, p]
+        L.oracle_rowwise_native_linear.argtypes = [p, p, p, p, p, i64, i64, i64, i32, p]
         L.oracle_f32_to_bf16_array.argtypes = [p, p, i64]
         L.oracle_f32_to_bf16_array.restype = None
         _LIB = L
@@ -160,6 +162,42 @@ def tokenwise_linear(a, a_scale, codes, w_scale, bias, fma: bool = True):
     out = np.empty((M, N), np.float32)
     _check(lib().oracle_tokenwise_linear(_ptr(a), _ptr(a_scale), _ptr(codes), _ptr(w_scale), _ptr(b), M, N, K,
                                          1 if fma else 0, _ptr(out)))
+    return out
+
+
+def quantize_rows_a4(x_bf16_bits):
+    """Per-row dynamic INT4 activations of a bf16 matrix (uint16 bits): packed [M, K/2]
+    u8 (even k in the low nibble) and scales [M] f32 (reference wxa4_native.py:27-64)."""
+    x = np.ascontiguousarray(x_bf16_bits, np.uint16)
+    M, K = x.shape
+    packed = np.empty((M, (K + 1) // 2), np.uint8)
+    scales = np.empty(M, np.float32)
+    _check(lib().oracle_quantize_rows_a4(_ptr(x), M, K, _ptr(packed), _ptr(scales)))
+    return packed, scales
+
+
+def unpack_a4(packed, K=None):
+    """Packed nibble rows [M, K/2] -> signed int8 codes [M, K] (even k low nibble)."""
+    p = np.ascontiguousarray(packed, np.uint8).astype(np.int16)
+    lo, hi = ((p & 15) ^ 8) - 8, (((p >> 4) & 15) ^ 8) - 8
+    out = np.stack([lo, hi], -1).reshape(p.shape[0], -1).astype(np.int8)
+    return out if K is None else out[:, :K]
+
+
+def rowwise_native_linear(a, a_scale, codes, w_scale, bias, fma: bool = True):
+    """Native W{2,4}A4 linear [M, N] f32: float(acc) * (as[m] * ws[n]) (+ bias), from
+    int8 activation codes [M, K] and weight codes [N, K]
+    (reference native_s4_extension_kernel.cu:226-234)."""
+    a = np.ascontiguousarray(a, np.int8)
+    codes = np.ascontiguousarray(codes, np.int8)
+    a_scale = np.ascontiguousarray(a_scale, np.float32)
+    w_scale = np.ascontiguousarray(w_scale, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    M, K = a.shape
+    N = codes.shape[0]
+    out = np.empty((M, N), np.float32)
+    _check(lib().oracle_rowwise_native_linear(_ptr(a), _ptr(a_scale), _ptr(codes), _ptr(w_scale), _ptr(b), M, N, K,
+                                              1 if fma else 0, _ptr(out)))
     return out
 
 

@@ -117,3 +117,37 @@ def test_tokenwise_matches_reference(tokenwise, w, si):
     assert bits_equal(y, g[f"{key}_out"])
     yf = O.tokenwise_linear(codes_a, scale, wq, ws, bias, fma=True)
     assert float(np.max(np.abs(yf - y))) <= 1e-6 * (float(np.abs(y).max()) + 1e-30)
+
+
+@pytest.fixture(scope="module")
+def wxa4():
+    return np.load(GOLDEN / "wxa4.npz")
+
+
+@pytest.mark.parametrize("w", [2, 4, 8])
+@pytest.mark.parametrize("si", [0, 1, 2])
+def test_wxa4_matches_reference(wxa4, w, si):
+    """Per-row A4 quantizer (packed nibbles, reciprocal-multiply scale) and its INT8
+    sign extension, the W{2,4} codebooks and the nested W8 code of W8A4, and the
+    W8A4 GEMM (the W8A8 Triton kernel on sign-extended A4 codes), against the
+    reference's W{2,4,8}A4NativeLinear run under the Triton interpreter."""
+    g, key = wxa4, f"w{w}_s{si}"
+    packed, scale = O.quantize_rows_a4(g[f"{key}_x"])
+    assert bits_equal(packed, g[f"{key}_packed"]) and bits_equal(scale, g[f"{key}_scale"])
+    act = O.unpack_a4(packed)
+    assert bits_equal(act, g[f"{key}_act"])
+    wq, ws = O.weight_codes(O.bf16_bits_to_f32(g[f"{key}_weight"]), w, 4)
+    assert bits_equal(wq, g[f"{key}_codes"]) and bits_equal(ws, g[f"{key}_ws"])
+    bias = g[f"{key}_bias"] if f"{key}_bias" in g else None
+    if w == 8:
+        y = O.tokenwise_linear(act, scale, wq, ws, bias, fma=False)  # interpreter: separate multiply and add
+        assert bits_equal(y, g[f"{key}_out"])
+    else:
+        # The native kernel's epilogue: float(acc) * (as * ws) (+ bias); against the
+        # exact product in float64 it stays within a few fp32 roundings.
+        y = O.rowwise_native_linear(act, scale, wq, ws, bias, fma=True)
+        acc = act.astype(np.int64) @ wq.astype(np.int64).T
+        ref = acc.astype(np.float64) * scale.astype(np.float64)[:, None] * ws.astype(np.float64)[None, :]
+        if bias is not None:
+            ref = ref + bias.astype(np.float64)[None, :]
+        assert np.abs(y - ref).max() <= 4e-7 * max(1.0, np.abs(ref).max())
