@@ -108,6 +108,7 @@ int pick_wt(int variant, int64_t M) {
 }
 
 bool is_wt_variant(int variant) { return variant >= ACTUNE_VARIANT_WT16 && variant <= ACTUNE_VARIANT_WT128; }
+bool is_x2_variant(int variant) { return variant >= ACTUNE_VARIANT_BN32X2 && variant <= ACTUNE_VARIANT_BN128X2; }
 
 // 3-D uint8 tensor map over a [rows, row_bytes] matrix (row_bytes a multiple of
 // 128) seen as (128-byte block, row, block index): a box of {128, box_rows,
@@ -146,6 +147,9 @@ int pick_bn(int variant, int64_t M, int64_t N, int num_sms) {
     case ACTUNE_VARIANT_BN32: return 32;
     case ACTUNE_VARIANT_BN64: return 64;
     case ACTUNE_VARIANT_BN128: return 128;
+    case ACTUNE_VARIANT_BN32X2: return 32;
+    case ACTUNE_VARIANT_BN64X2: return 64;
+    case ACTUNE_VARIANT_BN128X2: return 128;
     default: break;
   }
   // Minimise waves x per-tile time, modelled as (BN + 64) (a tile has a fixed
@@ -176,6 +180,16 @@ cudaError_t dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, co
 }
 
 template <int W, int A>
+cudaError_t dispatch_bn_x2(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
+                           cudaStream_t s) {
+  switch (bn) {
+    case 32: return launch_group64_gemm_x2<W, A, 32>(ta, tw, p, s);
+    case 64: return launch_group64_gemm_x2<W, A, 64>(ta, tw, p, s);
+    default: return launch_group64_gemm_x2<W, A, 128>(ta, tw, p, s);
+  }
+}
+
+template <int W, int A>
 cudaError_t dispatch_wt(int bt, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, cudaStream_t s) {
   switch (bt) {
     case 16: return launch_wt_gemm<W, A, 16>(ta, tw, p, s);
@@ -196,10 +210,10 @@ cudaError_t dispatch_wt_gemm(int W, int A, int bt, const CUtensorMap& ta, const 
   return cudaErrorInvalidValue;
 }
 
-cudaError_t dispatch_gemm(int W, int A, int bn, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
-                          cudaStream_t s) {
+cudaError_t dispatch_gemm(int W, int A, int bn, bool x2, const CUtensorMap& ta, const CUtensorMap& tw,
+                          const GemmParams& p, cudaStream_t s) {
 #define ACTUNE_CASE(WW, AA) \
-  if (W == WW && A == AA) return dispatch_bn<WW, AA>(bn, ta, tw, p, s);
+  if (W == WW && A == AA) return x2 ? dispatch_bn_x2<WW, AA>(bn, ta, tw, p, s) : dispatch_bn<WW, AA>(bn, ta, tw, p, s);
   ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
   ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
   ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
@@ -286,7 +300,10 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
   p.out_dtype = out_dtype;
   p.out_vec_ok = (N % 8 == 0) && aligned(out, 16);
-  const cudaError_t e = wt ? dispatch_wt_gemm(W, A, bn, ta, tw, p, stream) : dispatch_gemm(W, A, bn, ta, tw, p, stream);
+  // The debug dots export always runs the one-CTA-per-SM form.
+  const bool x2 = is_x2_variant(variant) && dots == nullptr;
+  const cudaError_t e =
+      wt ? dispatch_wt_gemm(W, A, bn, ta, tw, p, stream) : dispatch_gemm(W, A, bn, x2, ta, tw, p, stream);
   return cuda_status(e);
 }
 
@@ -385,7 +402,7 @@ int actune_packed_linear(const uint8_t* a, const float* a_scale, const uint8_t* 
                          int W, int A, int variant, void* stream) {
   int rc = check_gemm_shape(M, N, K, W, A);
   if (rc != ACTUNE_OK) return rc;
-  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_GEMV) return ACTUNE_ERR_INVALID_VALUE;
+  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_BN128X2) return ACTUNE_ERR_INVALID_VALUE;
   if (bias != nullptr && !valid_float_dtype(bias_dtype)) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && N > 0 && (a == nullptr || a_scale == nullptr || w == nullptr || w_scale == nullptr || out == nullptr))
     return ACTUNE_ERR_INVALID_VALUE;
@@ -473,7 +490,7 @@ int actune_packed_linear_dots(const uint8_t* a, const uint8_t* w, int32_t* dots,
                               int W, int A, int variant, void* stream) {
   int rc = check_gemm_shape(M, N, K, W, A);
   if (rc != ACTUNE_OK) return rc;
-  if (variant < 0 || variant > ACTUNE_VARIANT_GEMV) return ACTUNE_ERR_INVALID_VALUE;
+  if (variant < 0 || variant > ACTUNE_VARIANT_BN128X2) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && N > 0 && (a == nullptr || w == nullptr || dots == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
   if (!aligned(dots, 4)) return ACTUNE_ERR_MISALIGNED;
   return run_gemm(a, nullptr, w, nullptr, nullptr, kDtNone, nullptr, kDtF32, dots, M, N, K, W, A, variant,

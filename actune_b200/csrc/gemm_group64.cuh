@@ -46,20 +46,25 @@ struct GemmParams {
 // Wait-site identifiers recorded with a device timeout.
 enum : int { kSiteProducer = 1, kSiteConverter, kSiteMmaFull, kSiteMmaAcc, kSiteMmaDone, kSiteEpilogue, kSiteDrain };
 
-template <int W, int A, int BN>
+// OCC = CTAs resident per SM: 1, or 2 (half the TMEM columns, shared memory and
+// registers each, so that one CTA's MMA runs while the other's epilogue drains).
+template <int W, int A, int BN, int OCC = 1>
 struct Group64Cfg {
   static_assert(W == 2 || W == 4 || W == 8, "W");
   static_assert(A == 2 || A == 4 || A == 8, "A");
   static_assert(BN == 32 || BN == 64 || BN == 128, "BN");
+  static_assert(OCC == 1 || OCC == 2, "OCC");
   static constexpr int BM = 128;     // token rows per tile = TMEM lanes = MMA M
   static constexpr int KS = 128;     // K elements per pipeline stage (two groups)
   static constexpr int EPI_WG = 2;   // two epilogue warpgroups split the columns
   static constexpr int COLS = BN / EPI_WG;      // accumulator columns per epilogue thread
-  static constexpr int NPAIR = BN == 32 ? 4 : 2;   // accumulator buffer pairs (one pair per stage)
+  // Accumulator buffer pairs (one pair per stage): 512 TMEM columns per CTA, or 256
+  // at two CTAs per SM.
+  static constexpr int NPAIR = OCC == 1 ? (BN == 32 ? 4 : 2) : (BN == 128 ? 1 : 2);
   static constexpr int TMEM_COLS = NPAIR * 2 * BN; // 256 or 512 (power of two)
   static constexpr bool CONVERT = (A < 8) || (W < 8);
   // Warps: producer, MMA issuer, CVT_WARPS converters, then 4 * EPI_WG epilogue warps.
-  static constexpr int CVT_WARPS = CONVERT ? 4 : 0;
+  static constexpr int CVT_WARPS = CONVERT ? (OCC == 1 ? 4 : 2) : 0;
   static constexpr int EPI_WARP0 = 2 + CVT_WARPS;
   static constexpr int THREADS = 32 * EPI_WARP0 + 128 * EPI_WG;
   // Per-stage shared-memory layout: [act int8 | wgt int8 | act packed | wgt packed].
@@ -69,11 +74,15 @@ struct Group64Cfg {
   static constexpr int STG_W_BYTES = W < 8 ? BN * KS * W / 8 : 0;
   static constexpr int STAGE_RAW = OP_A_BYTES + OP_W_BYTES + STG_A_BYTES + STG_W_BYTES;
   static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
-  static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES_FIT = ((OCC == 1 ? 200 : 104) * 1024) / STAGE_BYTES;
   // A multiple of NPAIR, so that the accumulator pair of an unrolled ring slot is a
-  // compile-time constant.
-  static constexpr int STAGES = (STAGES_FIT > 8 ? 8 : STAGES_FIT) / NPAIR * NPAIR;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+  // compile-time constant, and even (the MMA issuer's two descriptor sets).
+  static constexpr int SLOT_MULT = NPAIR > 2 ? NPAIR : 2;
+  static constexpr int STAGES = (STAGES_FIT > 8 ? 8 : STAGES_FIT) / SLOT_MULT * SLOT_MULT;
+  // The final epilogue stages the fp32 tile [BM][BN + 4] through the ring.
+  static constexpr int OUT_STAGE_BYTES = BM * (BN + 4) * 4;
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES > OUT_STAGE_BYTES ? STAGES * STAGE_BYTES : OUT_STAGE_BYTES;
+  static constexpr int SMEM_BYTES = RING_BYTES + 1024;  // + alignment slack
   // Bytes one stage's two TMA loads deliver (full boxes; OOB parts are zero-filled).
   static constexpr uint32_t TX_BYTES = BM * KS * A / 8 + BN * KS * W / 8;
   // int8 operand value = code * 2^(8-bits): the dot carries 2^SHIFT.
@@ -189,11 +198,11 @@ __device__ __forceinline__ void store_dots(const GemmParams& p, int m, int col, 
 // TW (tokenwise backends): one full-K int32 accumulator per tile instead of one per
 // 64-group; the epilogue reads it once, converts it exactly (round to nearest) and
 // applies the per-token scale (p.act_scale[m]), then ws / bias as below.
-template <int W, int A, int BN, bool DOTS, bool TW = false>
-__global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
+template <int W, int A, int BN, bool DOTS, bool TW = false, int OCC = 1>
+__global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
     group64_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
                         const GemmParams p) {
-  using C = Group64Cfg<W, A, BN>;
+  using C = Group64Cfg<W, A, BN, OCC>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_raw[C::STAGES];
   __shared__ __align__(8) uint64_t full_op[C::STAGES];
@@ -577,6 +586,10 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
 template <int W, int A, int BN>
 cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
                                 cudaStream_t stream);
+// The same GEMM at two CTAs per SM (Group64Cfg OCC = 2).
+template <int W, int A, int BN>
+cudaError_t launch_group64_gemm_x2(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
+                                   cudaStream_t stream);
 // Row-scaled mode (per-token act_scale [M]; A = 8 tokenwise, A = 4 per-row A4).
 template <int W, int A, int BN>
 cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,

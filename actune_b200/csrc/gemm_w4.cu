@@ -23,6 +23,27 @@ cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm
   return cudaGetLastError();
 }
 
+// Two CTAs per SM (no debug-dots form: the one-CTA kernel exports dots).
+template <int W, int A, int BN>
+cudaError_t launch_group64_gemm_x2(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
+                                   cudaStream_t stream) {
+  using C = Group64Cfg<W, A, BN, 2>;
+  if (p.dots != nullptr) return cudaErrorInvalidValue;
+  auto kernel = group64_gemm_kernel<W, A, BN, false, false, 2>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const dim3 grid((p.M + C::BM - 1) / C::BM, (p.N + BN - 1) / BN);
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
+  return cudaGetLastError();
+}
+
 template <int W, int A, int BN>
 cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
                                      cudaStream_t stream) {
@@ -51,7 +72,9 @@ template cudaError_t launch_group64_tokenwise<4, 8, 128>(const CUtensorMap&, con
 
 #define ACTUNE_INST(A, BN)                                                                                  \
   template cudaError_t launch_group64_gemm<4, A, BN>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, \
-                                                     cudaStream_t);
+                                                     cudaStream_t);                                            \
+  template cudaError_t launch_group64_gemm_x2<4, A, BN>(const CUtensorMap&, const CUtensorMap&,                   \
+                                                        const GemmParams&, cudaStream_t);
 ACTUNE_INST(2, 32)
 ACTUNE_INST(2, 64)
 ACTUNE_INST(2, 128)

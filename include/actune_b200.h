@@ -67,7 +67,10 @@ typedef enum actune_variant {
   ACTUNE_VARIANT_WT32 = 5,
   ACTUNE_VARIANT_WT64 = 6,
   ACTUNE_VARIANT_WT128 = 7,
-  ACTUNE_VARIANT_GEMV = 8 /* weight-streaming kernel for M <= 32 (AUTO picks it there) */
+  ACTUNE_VARIANT_GEMV = 8, /* weight-streaming kernel for M <= 32 (AUTO picks it there) */
+  ACTUNE_VARIANT_BN32X2 = 9, /* BN* tiles at two CTAs per SM (half the tensor memory each) */
+  ACTUNE_VARIANT_BN64X2 = 10,
+  ACTUNE_VARIANT_BN128X2 = 11
 } actune_variant;
 
 /* Device error codes reported by actune_device_error(). */

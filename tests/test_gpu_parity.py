@@ -186,6 +186,19 @@ def test_gemm_random_bit_exact(ops, w, a, m, k, n):
 
 
 @pytest.mark.parametrize("w,a", PAIRS)
+@pytest.mark.parametrize("variant", [9, 10, 11])
+def test_gemm_two_ctas_per_sm_variants(ops, w, a, variant):
+    """BN32X2 / BN64X2 / BN128X2 (two CTAs per SM, half the tensor memory each, one
+    accumulator pair at BN=128) on ragged shapes and a multi-wave one: bit-exact, and
+    the debug dots export through them runs the one-CTA kernel."""
+    for m, k, n in [(37, 448, 200), (300, 1024, 1000)]:
+        y, ref, (pa, pw, pa_h) = _case(ops, m, k, n, w, a, seed=m + k + n + variant, variant=variant)
+        assert_bits(bf16_bits(y), O.to_bf16_bits(ref), f"bf16 output m={m} k={k} n={n}")
+    d = ops.packed_linear_dots(pa, pw, k, w, a, variant=variant)
+    assert torch.equal(d, ops.packed_linear_dots(pa, pw, k, w, a, variant=3))
+
+
+@pytest.mark.parametrize("w,a", PAIRS)
 @pytest.mark.parametrize("variant", [4, 5, 6, 7])
 def test_gemm_weights_in_tmem_variants(ops, w, a, variant):
     """The weights-in-TMEM kernel (explicit WT variants) on ragged shapes: partial
