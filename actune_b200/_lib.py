@@ -28,7 +28,8 @@ VARIANT_AUTO, VARIANT_BN32, VARIANT_BN64, VARIANT_BN128 = 0, 1, 2, 3
 VARIANT_WT16, VARIANT_WT32, VARIANT_WT64, VARIANT_WT128 = 4, 5, 6, 7
 VARIANT_GEMV = 8
 VARIANT_BN32X2, VARIANT_BN64X2, VARIANT_BN128X2 = 9, 10, 11
-VARIANT_MAX = VARIANT_BN128X2
+VARIANT_BN64P, VARIANT_BN128P = 12, 13
+VARIANT_MAX = VARIANT_BN128P
 
 # Every symbol the header declares (checked by the CPU test suite).
 EXPORTS = (

@@ -109,6 +109,15 @@ int pick_wt(int variant, int64_t M) {
 
 bool is_wt_variant(int variant) { return variant >= ACTUNE_VARIANT_WT16 && variant <= ACTUNE_VARIANT_WT128; }
 bool is_x2_variant(int variant) { return variant >= ACTUNE_VARIANT_BN32X2 && variant <= ACTUNE_VARIANT_BN128X2; }
+bool is_persistent_variant(int variant) {
+  return variant == ACTUNE_VARIANT_BN64P || variant == ACTUNE_VARIANT_BN128P;
+}
+
+// The persistent kernel stores 16-bit outputs with TMA: rows of N*2 bytes at a
+// 16-byte aligned base and pitch.
+bool persistent_ok(const void* out, int out_dtype, int64_t N) {
+  return (out_dtype == kDtBF16 || out_dtype == kDtF16) && N % 8 == 0 && N >= 64 && aligned(out, 16);
+}
 
 // 3-D uint8 tensor map over a [rows, row_bytes] matrix (row_bytes a multiple of
 // 128) seen as (128-byte block, row, block index): a box of {128, box_rows,
@@ -150,6 +159,8 @@ int pick_bn(int variant, int64_t M, int64_t N, int num_sms) {
     case ACTUNE_VARIANT_BN32X2: return 32;
     case ACTUNE_VARIANT_BN64X2: return 64;
     case ACTUNE_VARIANT_BN128X2: return 128;
+    case ACTUNE_VARIANT_BN64P: return 64;
+    case ACTUNE_VARIANT_BN128P: return 128;
     default: break;
   }
   // Minimise waves x per-tile time, modelled as (BN + 64) (a tile has a fixed
@@ -206,6 +217,28 @@ cudaError_t dispatch_wt_gemm(int W, int A, int bt, const CUtensorMap& ta, const 
   ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
   ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
   ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
+#undef ACTUNE_CASE
+  return cudaErrorInvalidValue;
+}
+
+template <int W, int A, bool TW>
+cudaError_t dispatch_persistent_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to,
+                                   const GemmParams& p, int num_sms, cudaStream_t s) {
+  return bn == 64 ? launch_group64_persistent<W, A, 64, TW>(ta, tw, to, p, num_sms, s)
+                  : launch_group64_persistent<W, A, 128, TW>(ta, tw, to, p, num_sms, s);
+}
+
+cudaError_t dispatch_persistent(int W, int A, bool tw_mode, int bn, const CUtensorMap& ta, const CUtensorMap& tw,
+                                const CUtensorMap& to, const GemmParams& p, int num_sms, cudaStream_t s) {
+#define ACTUNE_CASE(WW, AA)                                                                              \
+  if (W == WW && A == AA && !tw_mode) return dispatch_persistent_bn<WW, AA, false>(bn, ta, tw, to, p, num_sms, s);
+  ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
+  ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
+  ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
+#undef ACTUNE_CASE
+#define ACTUNE_CASE(WW, AA)                                                                             \
+  if (W == WW && A == AA && tw_mode) return dispatch_persistent_bn<WW, AA, true>(bn, ta, tw, to, p, num_sms, s);
+  ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
 #undef ACTUNE_CASE
   return cudaErrorInvalidValue;
 }
@@ -300,6 +333,12 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
   p.out_dtype = out_dtype;
   p.out_vec_ok = (N % 8 == 0) && aligned(out, 16);
+  if (!wt && dots == nullptr && is_persistent_variant(variant) && persistent_ok(out, out_dtype, N)) {
+    CUtensorMap to;
+    rc = encode_map(&to, out, M, N * 2, 128, 128, Swz::B128);
+    if (rc != ACTUNE_OK) return rc;
+    return cuda_status(dispatch_persistent(W, A, false, bn, ta, tw, to, p, g_devices[dev].num_sms, stream));
+  }
   // The debug dots export always runs the one-CTA-per-SM form.
   const bool x2 = is_x2_variant(variant) && dots == nullptr;
   const cudaError_t e =
@@ -347,6 +386,12 @@ int run_rowwise(const uint8_t* a, int A, const float* a_scale, const uint8_t* w,
   if (rc != ACTUNE_OK) return rc;
   p.G = (int)((K + 63) / 64);  // stages of 128 codes; the zero fill past K adds nothing
   p.out_vec_ok = (N % 8 == 0) && aligned(out, 16);
+  if (is_persistent_variant(variant) && persistent_ok(out, out_dtype, N)) {
+    CUtensorMap to;
+    rc = encode_map(&to, out, M, N * 2, 128, 128, Swz::B128);
+    if (rc != ACTUNE_OK) return rc;
+    return cuda_status(dispatch_persistent(W, A, true, bn, ta, tw, to, p, g_devices[dev].num_sms, stream));
+  }
   cudaError_t e = cudaErrorInvalidValue;
 #define ACTUNE_TW(WW, AA)                                                              \
   if (W == WW && A == AA) {                                                            \
@@ -402,7 +447,7 @@ int actune_packed_linear(const uint8_t* a, const float* a_scale, const uint8_t* 
                          int W, int A, int variant, void* stream) {
   int rc = check_gemm_shape(M, N, K, W, A);
   if (rc != ACTUNE_OK) return rc;
-  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_BN128X2) return ACTUNE_ERR_INVALID_VALUE;
+  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_BN128P) return ACTUNE_ERR_INVALID_VALUE;
   if (bias != nullptr && !valid_float_dtype(bias_dtype)) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && N > 0 && (a == nullptr || a_scale == nullptr || w == nullptr || w_scale == nullptr || out == nullptr))
     return ACTUNE_ERR_INVALID_VALUE;
@@ -450,7 +495,8 @@ int actune_tokenwise_linear(const int8_t* a, const float* a_scale, const uint8_t
   if (!valid_bits(W) || K <= 0 || K % 64 || K > (int64_t(1) << 24) || M < 0 || N < 0 || M >= (int64_t(1) << 31) ||
       N >= (int64_t(1) << 31))
     return ACTUNE_ERR_INVALID_VALUE;
-  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_BN128) return ACTUNE_ERR_INVALID_VALUE;
+  if (!valid_float_dtype(out_dtype) || variant < 0 || (variant > ACTUNE_VARIANT_BN128 && !is_persistent_variant(variant)))
+    return ACTUNE_ERR_INVALID_VALUE;
   if (bias != nullptr && !valid_float_dtype(bias_dtype)) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && N > 0 && (a == nullptr || a_scale == nullptr || w == nullptr || w_scale == nullptr || out == nullptr))
     return ACTUNE_ERR_INVALID_VALUE;
@@ -471,7 +517,8 @@ int actune_rowwise_linear(const uint8_t* a, int A, const float* a_scale, const u
   if (!valid_bits(W) || (A != 4 && A != 8) || (order != 0 && order != 1) || K <= 0 || K % 64 ||
       K > (int64_t(1) << 24) || M < 0 || N < 0 || M >= (int64_t(1) << 31) || N >= (int64_t(1) << 31))
     return ACTUNE_ERR_INVALID_VALUE;
-  if (!valid_float_dtype(out_dtype) || variant < 0 || variant > ACTUNE_VARIANT_BN128) return ACTUNE_ERR_INVALID_VALUE;
+  if (!valid_float_dtype(out_dtype) || variant < 0 || (variant > ACTUNE_VARIANT_BN128 && !is_persistent_variant(variant)))
+    return ACTUNE_ERR_INVALID_VALUE;
   if (bias != nullptr && !valid_float_dtype(bias_dtype)) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && N > 0 && (a == nullptr || a_scale == nullptr || w == nullptr || w_scale == nullptr || out == nullptr))
     return ACTUNE_ERR_INVALID_VALUE;
@@ -490,7 +537,7 @@ int actune_packed_linear_dots(const uint8_t* a, const uint8_t* w, int32_t* dots,
                               int W, int A, int variant, void* stream) {
   int rc = check_gemm_shape(M, N, K, W, A);
   if (rc != ACTUNE_OK) return rc;
-  if (variant < 0 || variant > ACTUNE_VARIANT_BN128X2) return ACTUNE_ERR_INVALID_VALUE;
+  if (variant < 0 || variant > ACTUNE_VARIANT_BN128P) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && N > 0 && (a == nullptr || w == nullptr || dots == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
   if (!aligned(dots, 4)) return ACTUNE_ERR_MISALIGNED;
   return run_gemm(a, nullptr, w, nullptr, nullptr, kDtNone, nullptr, kDtF32, dots, M, N, K, W, A, variant,

@@ -590,6 +590,12 @@ cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm
 template <int W, int A, int BN>
 cudaError_t launch_group64_gemm_x2(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
                                    cudaStream_t stream);
+// Persistent form (gemm_group64_persistent.cuh): bf16 / f16 output through a TMA
+// store map `tm_out` (uint8 view of [M, N*2] bytes, box 128 B x 128 rows, 128B
+// swizzle); BN 64 or 128; TW selects the row-scaled mode.
+template <int W, int A, int BN, bool TW>
+cudaError_t launch_group64_persistent(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const CUtensorMap& tm_out,
+                                      const GemmParams& p, int num_sms, cudaStream_t stream);
 // Row-scaled mode (per-token act_scale [M]; A = 8 tokenwise, A = 4 per-row A4).
 template <int W, int A, int BN>
 cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,

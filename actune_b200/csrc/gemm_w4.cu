@@ -1,5 +1,5 @@
 // Instantiations of the group-64 tcgen05 GEMM for W = 4 (all A, all tile widths).
-#include "gemm_group64.cuh"
+#include "gemm_group64_persistent.cuh"
 
 namespace actune {
 
@@ -69,6 +69,42 @@ template cudaError_t launch_group64_tokenwise<4, 4, 128>(const CUtensorMap&, con
 template cudaError_t launch_group64_tokenwise<4, 8, 32>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
 template cudaError_t launch_group64_tokenwise<4, 8, 64>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
 template cudaError_t launch_group64_tokenwise<4, 8, 128>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+
+template <int W, int A, int BN, bool TW>
+cudaError_t launch_group64_persistent(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const CUtensorMap& tm_out,
+                                      const GemmParams& p, int num_sms, cudaStream_t stream) {
+  using C = PersistCfg<W, A, BN, TW>;
+  auto kernel = group64_gemm_persistent_kernel<W, A, BN, TW>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const int tiles = ((p.M + 127) / 128) * ((p.N + BN - 1) / BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  kernel<<<grid, Group64Cfg<W, A, BN>::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, tm_out, p);
+  return cudaGetLastError();
+}
+
+#define ACTUNE_PERSIST(A, BN, TW)                                                                             \
+  template cudaError_t launch_group64_persistent<4, A, BN, TW>(const CUtensorMap&, const CUtensorMap&,     \
+                                                               const CUtensorMap&, const GemmParams&, int,   \
+                                                               cudaStream_t);
+ACTUNE_PERSIST(2, 64, false)
+ACTUNE_PERSIST(2, 128, false)
+ACTUNE_PERSIST(4, 64, false)
+ACTUNE_PERSIST(4, 128, false)
+ACTUNE_PERSIST(8, 64, false)
+ACTUNE_PERSIST(8, 128, false)
+ACTUNE_PERSIST(4, 64, true)
+ACTUNE_PERSIST(4, 128, true)
+ACTUNE_PERSIST(8, 64, true)
+ACTUNE_PERSIST(8, 128, true)
+#undef ACTUNE_PERSIST
 
 #define ACTUNE_INST(A, BN)                                                                                  \
   template cudaError_t launch_group64_gemm<4, A, BN>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, \

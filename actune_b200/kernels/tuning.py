@@ -75,6 +75,7 @@ def grouped_forward(self, x):
                                  out_dtype=x.dtype, variant=variant)
 
     configs = [_lib.VARIANT_AUTO, _lib.VARIANT_BN32, _lib.VARIANT_BN64, _lib.VARIANT_BN128,
-               _lib.VARIANT_BN32X2, _lib.VARIANT_BN64X2, _lib.VARIANT_BN128X2]
+               _lib.VARIANT_BN32X2, _lib.VARIANT_BN64X2, _lib.VARIANT_BN128X2,
+               _lib.VARIANT_BN64P, _lib.VARIANT_BN128P]
     key = ("grouped", self.w, self.a, m, k, n, str(x.dtype), self.bias is not None)
     return launch(select(key, launch, configs, _lib.VARIANT_AUTO)).reshape(*x.shape[:-1], n)

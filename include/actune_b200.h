@@ -70,7 +70,9 @@ typedef enum actune_variant {
   ACTUNE_VARIANT_GEMV = 8, /* weight-streaming kernel for M <= 32 (AUTO picks it there) */
   ACTUNE_VARIANT_BN32X2 = 9, /* BN* tiles at two CTAs per SM (half the tensor memory each) */
   ACTUNE_VARIANT_BN64X2 = 10,
-  ACTUNE_VARIANT_BN128X2 = 11
+  ACTUNE_VARIANT_BN128X2 = 11,
+  ACTUNE_VARIANT_BN64P = 12, /* BN64 / BN128 tiles in a persistent kernel (one CTA per SM walking the tiles, */
+  ACTUNE_VARIANT_BN128P = 13 /* TMA-store epilogue); bf16/f16 outputs with N % 8 == 0, else the BN kernel */
 } actune_variant;
 
 /* Device error codes reported by actune_device_error(). */

@@ -199,6 +199,26 @@ def test_gemm_two_ctas_per_sm_variants(ops, w, a, variant):
 
 
 @pytest.mark.parametrize("w,a", PAIRS)
+@pytest.mark.parametrize("variant", [12, 13])
+def test_gemm_persistent_variants(ops, w, a, variant):
+    """BN64P / BN128P (one CTA per SM walking the tiles, TMA-store epilogue): ragged
+    tiles, an odd number of K groups, more tiles than SMs (each CTA takes several),
+    bf16 and f16 outputs bit-exact; fp32 outputs and N % 8 != 0 fall back to the
+    one-tile kernel."""
+    for m, k, n, out_dtype in [(37, 448, 200, torch.bfloat16), (300, 1024, 1000, torch.float16),
+                               (600, 2048, 4096, torch.bfloat16), (129, 192, 136, torch.float32),
+                               (70, 256, 100, torch.bfloat16)]:
+        y, ref, _ = _case(ops, m, k, n, w, a, seed=m + k + n + variant, out_dtype=out_dtype, variant=variant)
+        if out_dtype == torch.float32:
+            assert_bits(y.numpy(), ref, f"fp32 output m={m} k={k} n={n}")
+        elif out_dtype == torch.float16:
+            assert_bits(y.view(torch.int16).numpy().view(np.uint16), ref.astype(np.float16).view(np.uint16),
+                        f"f16 output m={m} k={k} n={n}")
+        else:
+            assert_bits(bf16_bits(y), O.to_bf16_bits(ref), f"bf16 output m={m} k={k} n={n}")
+
+
+@pytest.mark.parametrize("w,a", PAIRS)
 @pytest.mark.parametrize("variant", [4, 5, 6, 7])
 def test_gemm_weights_in_tmem_variants(ops, w, a, variant):
     """The weights-in-TMEM kernel (explicit WT variants) on ragged shapes: partial

@@ -64,7 +64,7 @@ def test_tokenwise_golden(ops, tw, w, si):
     k = x.shape[1]
     ref = O.tokenwise_linear(tw[f"{key}_act"], tw[f"{key}_scale"], tw[f"{key}_codes"], tw[f"{key}_ws"],
                              O.bf16_bits_to_f32(tw[f"{key}_bias"]) if has_bias else None, fma=True)
-    for variant in (0, 1, 2, 3):
+    for variant in (0, 1, 2, 3, 12, 13):  # AUTO, BN32/64/128, persistent BN64P/BN128P
         y = ops.tokenwise_linear(act, scale, rows, ws, bias, k, w, out_dtype=torch.float32, variant=variant)
         assert bits_equal(y.cpu().numpy(), ref), f"fp32 variant {variant}"
         yb = ops.tokenwise_linear(act, scale, rows, ws, bias, k, w, out_dtype=torch.bfloat16, variant=variant)

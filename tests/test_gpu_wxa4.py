@@ -76,7 +76,7 @@ def test_wxa4_golden(ops, g, w, si):
     bias = torch.from_numpy(bias_np).to(DEV) if has_bias else None
     k = x.shape[1]
     ref = oracle_out(w, g[f"{key}_act"], g[f"{key}_scale"], codes, g[f"{key}_ws"], bias_np)
-    for variant in (0, 1, 2, 3):
+    for variant in (0, 1, 2, 3, 12, 13):  # AUTO, BN32/64/128, persistent BN64P/BN128P
         y = ops.rowwise_linear(packed, 4, scale, rows, w, ws, bias, k, order=order_of(ops, w),
                                out_dtype=torch.float32, variant=variant)
         assert bits_equal(y.cpu().numpy(), ref), f"fp32 variant {variant}"
