@@ -409,9 +409,10 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
     const int m = m0 + row;
     const bool warp_live = (m0 + q * 32) < p.M;  // any valid token row in this warp
     const int col0 = n0 + e * C::COLS;
-    // TMEM is read in P parts of H columns per group: quarters when converter warps
-    // share the register file, halves otherwise.
-    constexpr int P = C::CVT_WARPS > 0 && C::COLS >= 16 ? 4 : 2;
+    // TMEM is read in P parts of H columns per group: eight parts (four for narrow
+    // tiles) when converter warps share the register file, four otherwise (measured
+    // best; the part size moves the GEMM by a few percent at most).
+    constexpr int P = C::CVT_WARPS > 0 ? (C::COLS >= 64 ? 8 : C::COLS >= 16 ? 4 : 2) : (C::COLS >= 16 ? 4 : 2);
     constexpr int H = C::COLS / P;
     const float shift_scale = 1.0f / float(1 << C::SHIFT);
     const bool load_scales = !DOTS && warp_live && m < p.M;

@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN>::THREADS, 1)
     const int row = q * 32 + lane;
     const bool issuer = ew == 0 && lane == 0;
     constexpr int COLS = B::COLS;
-    constexpr int P = B::CVT_WARPS > 0 && COLS >= 16 ? 4 : 2;
+    constexpr int P = B::CVT_WARPS > 0 ? (COLS >= 64 ? 8 : COLS >= 16 ? 4 : 2) : (COLS >= 16 ? 4 : 2);
     constexpr int H = COLS / P;
     const float shift_scale = 1.0f / float(1 << B::SHIFT);
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + e * COLS;
