@@ -208,3 +208,15 @@ def test_clip_ratio_validation_messages():
         _validate_clip_ratios(float("nan"), out_features=4, device="cpu")
     with pytest.raises(ValueError, match=r"\(0, 1\]"):
         _validate_clip_ratios(1.5, out_features=4, device="cpu")
+
+
+def test_sweep_table_and_workload():
+    """The config-1 sweep covers the 4 Llama-2-7B projection shapes and formats one
+    markdown row per case (no GPU needed to check the host side)."""
+    from actune_b200 import sweep
+    assert sweep.SHAPES == {"qkv": (4096, 12288), "o": (4096, 4096), "gate_up": (4096, 22016),
+                            "down": (11008, 4096)}
+    row = {"W": 4, "A": 8, "shape": "qkv", "M": 1, "K": 4096, "N": 12288, "us": 14.5, "GBps": 1740.0,
+           "hbm_frac": 0.27, "TOPS": 6.9, "int8_frac": 0.002}
+    text = sweep.markdown({"hbm_gbs": 6456.8, "int8_tops": 3021.0, "rows": [row]})
+    assert "| W4A8 | qkv | 1 | 14.5 | 1740.0 | 0.27 | 6.9 | 0.002 |" in text
