@@ -294,7 +294,8 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return _
 
 // Exact int32 -> fp32 for |v| < 2^22: the bit pattern 0x4B400000 + v is the
 // binary32 number 1.5*2^23 + v (ulp 1 in that binade); subtracting 1.5*2^23
-// afterwards is exact.  Replaces the quarter-rate I2F conversion.
+// afterwards is exact.  Used by the decode and weights-in-TMEM kernels; the
+// group-64 GEMM epilogue measured faster with the hardware conversion.
 constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagicValue = 12582912.0f;
 

@@ -174,12 +174,12 @@ __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
 // acc[j] += float(d[2j..2j+1]) * s for H int32 dots (exact conversion, packed fp32x2 FMA).
 template <int H>
 __device__ __forceinline__ void accumulate(float2* acc, const uint32_t (&d)[H], float s) {
+  // float(dot) exactly (|dot * 2^SHIFT| < 2^24): the hardware conversion measured
+  // 4-7% faster here than the two-instruction bit-pattern form.
   const float2 s2 = make_float2(s, s);
-  const float2 magic = make_float2(-kMagicValue, -kMagicValue);
 #pragma unroll
   for (int j = 0; j < H / 2; ++j) {
-    float2 f = make_float2(__uint_as_float(d[2 * j] + kMagicBits), __uint_as_float(d[2 * j + 1] + kMagicBits));
-    f = fadd2(f, magic);
+    const float2 f = make_float2(__int2float_rn((int)d[2 * j]), __int2float_rn((int)d[2 * j + 1]));
     acc[j] = ffma2(f, s2, acc[j]);
   }
 }
