@@ -278,12 +278,13 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
     const bool whole = M <= 16 && (K * A / 8) % 128 == 0 && (K * W / 8) % 128 == 0 &&
                        (dots != nullptr || ((K / 64) % 4 == 0 && aligned(a_scale, 16)));
     if (whole) {
-      rc = encode_map_blocks(&ta, a, M, K * A / 8, (int)M, kGemvStageK * A / 8 / 128);
+      const int sk = gemv_wide(M, W, dots != nullptr) ? kGemvStageKWide : kGemvStageK;
+      rc = encode_map_blocks(&ta, a, M, K * A / 8, (int)M, sk * A / 8 / 128);
       if (rc != ACTUNE_OK) return rc;
-      rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, kGemvStageK * W / 8 / 128);
+      rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, sk * W / 8 / 128);
       if (rc != ACTUNE_OK) return rc;
       ts = ta;  // never read by the dots export
-      if (dots == nullptr) rc = encode_map_f32(&ts, a_scale, M, K / 64, 16, (int)M);
+      if (dots == nullptr) rc = encode_map_f32(&ts, a_scale, M, K / 64, sk / 64, (int)M);
     } else {
       rc = encode_map(&ta, a, M, K * A / 8, 128, tok, Swz::B128);
       if (rc != ACTUNE_OK) return rc;
@@ -371,9 +372,10 @@ int run_rowwise(const uint8_t* a, int A, const float* a_scale, const uint8_t* w,
   CUtensorMap ta, tw;
   if (variant == ACTUNE_VARIANT_AUTO && M <= 16 && (K * A / 8) % 128 == 0 && (K * W / 8) % 128 == 0) {
     // Decode sizes: the weight-streaming kernel in its row-scaled mode.
-    rc = encode_map_blocks(&ta, a, M, K * A / 8, (int)M, kGemvStageK * A / 8 / 128);
+    const int sk = gemv_wide(M, W, false) ? kGemvStageKWide : kGemvStageK;
+    rc = encode_map_blocks(&ta, a, M, K * A / 8, (int)M, sk * A / 8 / 128);
     if (rc != ACTUNE_OK) return rc;
-    rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, kGemvStageK * W / 8 / 128);
+    rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, sk * W / 8 / 128);
     if (rc != ACTUNE_OK) return rc;
     p.G = (int)(K / 64);
     p.out_vec_ok = 0;

@@ -311,9 +311,11 @@ __device__ __forceinline__ uint32_t swizzled_offset(int gl, int t, int r, int bo
 // is stored and read.  Shared-memory traffic per stage is what bounds this kernel
 // (the copies, the token fragments and the dot round trip share 128 B/clk).
 // A stage slot is free once the 16 dot warps and the 4 chain warps released it.
-template <int W, int A, bool HI>
+template <int W, int A, bool HI, bool WIDE = false>
 struct Gemv4Cfg {
-  static constexpr int ROWS = 32, TOK = HI ? 16 : 8, KSTG = 1024, GPS = 16, QL = 8, GPQ = GPS / QL;
+  static_assert(!WIDE || (!HI && W <= 4), "wide stages: at most 8 tokens, 2- or 4-bit weights");
+  static constexpr int ROWS = 32, TOK = HI ? 16 : 8, KSTG = WIDE ? kGemvStageKWide : kGemvStageK;
+  static constexpr int GPS = KSTG / 64, QL = 8, GPQ = GPS / QL;
   static constexpr int DOT_WARPS = 16, CHAIN_WARPS = 4, PRODUCER = DOT_WARPS + CHAIN_WARPS;
   static constexpr int THREADS = 32 * (PRODUCER + 1);
   static constexpr int A_BLK = KSTG * A / 8 / 128;
@@ -342,11 +344,11 @@ enum : int { kGv4SiteFull = 61, kGv4SiteEmpty, kGv4SiteDotFull, kGv4SiteDotEmpty
 // TW (tokenwise backends): no per-group scales; the dot buffers carry the raw int32
 // dots, the chain warps add them exactly and apply float(acc) * as[m] * ws (+ bias)
 // once per row block (as: one scale per token).
-template <int W, int A, bool HI, bool DOTS, bool TW = false>
-__global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
+template <int W, int A, bool HI, bool DOTS, bool TW = false, bool WIDE = false>
+__global__ void __launch_bounds__(Gemv4Cfg<W, A, HI, WIDE>::THREADS, 1)
     gemv4_group64_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
                          const __grid_constant__ CUtensorMap tm_scale, const GemmParams p) {
-  using C = Gemv4Cfg<W, A, HI>;
+  using C = Gemv4Cfg<W, A, HI, WIDE>;
   using DotT = typename std::conditional<HI, float4, float2>::type;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
@@ -575,13 +577,19 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI>::THREADS, 1)
   }
 }
 
-template <int W, int A, bool HI, bool TW = false>
+template <int W, int A, bool HI, bool TW = false, bool WIDE = false>
 static cudaError_t launch_gemv4_hi(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
                                    const GemmParams& p, int num_sms, cudaStream_t stream) {
-  using C = Gemv4Cfg<W, A, HI>;
+  using C = Gemv4Cfg<W, A, HI, WIDE>;
   const bool dots = !TW && p.dots != nullptr;
-  auto kernel = TW ? gemv4_group64_kernel<W, A, HI, false, TW>
-                   : (dots ? gemv4_group64_kernel<W, A, HI, true> : gemv4_group64_kernel<W, A, HI, false>);
+  void (*kernel)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
+  if constexpr (WIDE) {
+    if (dots) return cudaErrorInvalidValue;  // the dots export runs 1024-K stages
+    kernel = gemv4_group64_kernel<W, A, HI, false, TW, true>;
+  } else {
+    kernel = TW ? gemv4_group64_kernel<W, A, HI, false, TW>
+                : (dots ? gemv4_group64_kernel<W, A, HI, true> : gemv4_group64_kernel<W, A, HI, false>);
+  }
   int dev = 0;
   cudaGetDevice(&dev);
   static bool configured[2][64] = {};
@@ -600,8 +608,19 @@ static cudaError_t launch_gemv4_hi(const CUtensorMap& ta, const CUtensorMap& tw,
 template <int W, int A>
 static cudaError_t launch_gemv4_t(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& ts,
                                   const GemmParams& p, int num_sms, cudaStream_t stream) {
-  return p.M > 8 ? launch_gemv4_hi<W, A, true>(ta, tw, ts, p, num_sms, stream)
-                 : launch_gemv4_hi<W, A, false>(ta, tw, ts, p, num_sms, stream);
+  if (p.M > 8) return launch_gemv4_hi<W, A, true>(ta, tw, ts, p, num_sms, stream);
+  if constexpr (W <= 4)
+    if (gemv_wide(p.M, W, p.dots != nullptr)) return launch_gemv4_hi<W, A, false, false, true>(ta, tw, ts, p, num_sms, stream);
+  return launch_gemv4_hi<W, A, false>(ta, tw, ts, p, num_sms, stream);
+}
+
+template <int W, int A>
+static cudaError_t launch_gemv4_rowwise(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, int num_sms,
+                                        cudaStream_t stream) {
+  if (p.M > 8) return launch_gemv4_hi<W, A, true, true>(ta, tw, ta, p, num_sms, stream);
+  if constexpr (W <= 4)
+    if (gemv_wide(p.M, W, false)) return launch_gemv4_hi<W, A, false, true, true>(ta, tw, ta, p, num_sms, stream);
+  return launch_gemv4_hi<W, A, false, true>(ta, tw, ta, p, num_sms, stream);
 }
 
 template <int W, int A, int MT>
@@ -642,10 +661,8 @@ cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUten
 // its TW mode.
 cudaError_t launch_gemv_tokenwise(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
                                   int num_sms, cudaStream_t stream) {
-#define ACTUNE_CASE(WW, AA)                                                                \
-  if (W == WW && A == AA)                                                                  \
-    return p.M > 8 ? launch_gemv4_hi<WW, AA, true, true>(ta, tw, ta, p, num_sms, stream)   \
-                   : launch_gemv4_hi<WW, AA, false, true>(ta, tw, ta, p, num_sms, stream);
+#define ACTUNE_CASE(WW, AA) \
+  if (W == WW && A == AA) return launch_gemv4_rowwise<WW, AA>(ta, tw, p, num_sms, stream);
   ACTUNE_CASE(2, 8) ACTUNE_CASE(4, 8) ACTUNE_CASE(8, 8)
   ACTUNE_CASE(2, 4) ACTUNE_CASE(4, 4) ACTUNE_CASE(8, 4)
 #undef ACTUNE_CASE

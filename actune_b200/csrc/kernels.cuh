@@ -23,6 +23,10 @@ cudaError_t launch_r4_refine(const void* w, int dtype, int64_t N, int64_t K, con
 // Without: 2-D maps with 128-byte-wide boxes of 16 * ceil(M / 16) token rows and 32
 // weight rows.  Packed boxes use the 128-byte swizzle.
 constexpr int kGemvStageK = 1024;
+// Up to 4 tokens and 2- or 4-bit weights: stages of 2048 K (measured 4-16% faster at
+// M = 1; slower at M = 8, where the chain work per stage doubles).
+constexpr int kGemvStageKWide = 2048;
+inline bool gemv_wide(int64_t M, int W, bool dots) { return M <= 4 && W <= 4 && !dots; }
 // Tokenwise decode (M <= 16, K*W/8 and K multiples of 128 bytes): whole-stage maps as
 // above, no scale map; p.act_scale holds one scale per token.
 cudaError_t launch_gemv_tokenwise(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
