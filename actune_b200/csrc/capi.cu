@@ -273,15 +273,22 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
     if (M > 32) return ACTUNE_ERR_INVALID_VALUE;
     CUtensorMap ta, tw, ts;
     const int tok = M <= 16 ? 16 : 32;
-    // Whole-stage boxes need 128-byte packed rows and, for the scale tile, 16-byte
-    // scale rows at a 16-byte aligned base.
-    const bool whole = M <= 16 && (K * A / 8) % 128 == 0 && (K * W / 8) % 128 == 0 &&
-                       (dots != nullptr || ((K / 64) % 4 == 0 && aligned(a_scale, 16)));
+    // The split-role kernel loads the stage's activation scales as a tile: 16-byte
+    // scale rows at a 16-byte aligned base.  Packed rows of whole 128-byte blocks
+    // load as one 3-D box per operand, other rows as one 2-D box per block.
+    const bool whole = M <= 16 && (dots != nullptr || ((K / 64) % 4 == 0 && aligned(a_scale, 16)));
+    const bool boxes2d = (K * A / 8) % 128 != 0 || (K * W / 8) % 128 != 0;
     if (whole) {
       const int sk = gemv_wide(M, W, dots != nullptr) ? kGemvStageKWide : kGemvStageK;
-      rc = encode_map_blocks(&ta, a, M, K * A / 8, (int)M, sk * A / 8 / 128);
-      if (rc != ACTUNE_OK) return rc;
-      rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, sk * W / 8 / 128);
+      if (boxes2d) {
+        rc = encode_map(&ta, a, M, K * A / 8, 128, M > 8 ? 16 : 8, Swz::B128);
+        if (rc != ACTUNE_OK) return rc;
+        rc = encode_map(&tw, w, N, K * W / 8, 128, kGemvRows, Swz::B128);
+      } else {
+        rc = encode_map_blocks(&ta, a, M, K * A / 8, (int)M, sk * A / 8 / 128);
+        if (rc != ACTUNE_OK) return rc;
+        rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, sk * W / 8 / 128);
+      }
       if (rc != ACTUNE_OK) return rc;
       ts = ta;  // never read by the dots export
       if (dots == nullptr) rc = encode_map_f32(&ts, a_scale, M, K / 64, sk / 64, (int)M);
@@ -304,6 +311,7 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
     p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
     p.out_dtype = out_dtype;
     p.out_vec_ok = 0;
+    p.gemv_boxes2d = whole && boxes2d;
     return cuda_status(launch_gemv_group64(W, A, ta, tw, whole ? &ts : nullptr, p, g_devices[dev].num_sms, stream));
   }
   const bool wt = is_wt_variant(variant);
@@ -370,12 +378,20 @@ int run_rowwise(const uint8_t* a, int A, const float* a_scale, const uint8_t* w,
   p.out_dtype = out_dtype;
   p.rowwise_order = order;
   CUtensorMap ta, tw;
-  if (variant == ACTUNE_VARIANT_AUTO && M <= 16 && (K * A / 8) % 128 == 0 && (K * W / 8) % 128 == 0) {
-    // Decode sizes: the weight-streaming kernel in its row-scaled mode.
+  if (variant == ACTUNE_VARIANT_AUTO && M <= 16) {
+    // Decode sizes: the weight-streaming kernel in its row-scaled mode (3-D boxes for
+    // rows of whole 128-byte blocks, else one 2-D box per block).
     const int sk = gemv_wide(M, W, false) ? kGemvStageKWide : kGemvStageK;
-    rc = encode_map_blocks(&ta, a, M, K * A / 8, (int)M, sk * A / 8 / 128);
-    if (rc != ACTUNE_OK) return rc;
-    rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, sk * W / 8 / 128);
+    p.gemv_boxes2d = (K * A / 8) % 128 != 0 || (K * W / 8) % 128 != 0;
+    if (p.gemv_boxes2d) {
+      rc = encode_map(&ta, a, M, K * A / 8, 128, M > 8 ? 16 : 8, Swz::B128);
+      if (rc != ACTUNE_OK) return rc;
+      rc = encode_map(&tw, w, N, K * W / 8, 128, kGemvRows, Swz::B128);
+    } else {
+      rc = encode_map_blocks(&ta, a, M, K * A / 8, (int)M, sk * A / 8 / 128);
+      if (rc != ACTUNE_OK) return rc;
+      rc = encode_map_blocks(&tw, w, N, K * W / 8, kGemvRows, sk * W / 8 / 128);
+    }
     if (rc != ACTUNE_OK) return rc;
     p.G = (int)(K / 64);
     p.out_vec_ok = 0;

@@ -41,6 +41,7 @@ struct GemmParams {
   int out_dtype;
   int out_vec_ok;          // N % 8 == 0 and out 16-byte aligned
   int rowwise_order;       // row-scaled modes: 0 (acc*as)*ws, 1 acc*(as*ws) (the per-row A4 native order)
+  int gemv_boxes2d;        // decode: packed rows not whole 128-byte blocks, one 2-D box per block
 };
 
 // Wait-site identifiers recorded with a device timeout.

@@ -382,10 +382,21 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI, WIDE>::THREADS, 1)
   if (warp == C::PRODUCER) {
     // ------------------------------------------------------------ producer
     // Lanes 0 (weights), 1 (tokens) and 2 (scales) issue a stage's three boxes in
-    // one instruction.
-    if (lane < 3) {
-      prefetch_tensormap(lane == 0 ? &tm_wgt : lane == 1 ? &tm_act : &tm_scale);
-      const uint32_t stage_tx = C::W_BYTES + Mb * (C::A_BLK * 128 + ((DOTS || TW) ? 0 : C::GPS * 4));
+    // one instruction.  When the packed rows are not whole 128-byte blocks the
+    // maps are 2-D and every 128-byte block is a box of its own: lanes
+    // 0..W_BLK-1 the weight blocks, the next A_BLK lanes the token blocks (TOK rows
+    // high, so that the swizzle phase of a line is its row), then the scales; the
+    // part of a block past the row end is the TMA's zero fill.
+    const bool b2d = p.gemv_boxes2d != 0;
+    const int lanes = b2d ? C::W_BLK + C::A_BLK + 1 : 3;
+    static_assert(C::W_BLK + C::A_BLK + 1 <= 32, "one lane per block");
+    if (lane < lanes) {
+      const int kind = b2d ? (lane < C::W_BLK ? 0 : lane < C::W_BLK + C::A_BLK ? 1 : 2) : lane;
+      const int blk = b2d ? (kind == 0 ? lane : lane - C::W_BLK) : 0;
+      if (blk == 0) prefetch_tensormap(kind == 0 ? &tm_wgt : kind == 1 ? &tm_act : &tm_scale);
+      const uint32_t mask = lanes == 32 ? 0xffffffffu : ((1u << lanes) - 1u);
+      const uint32_t stage_tx = C::W_BYTES + (b2d ? C::A_BLK * C::TOK * 128 : Mb * C::A_BLK * 128) +
+                                ((DOTS || TW) ? 0 : Mb * C::GPS * 4);
       int issued = 0;
       for (int it = 0; it < total; ++it) {
         const int s = it % C::STAGES;
@@ -394,12 +405,22 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI, WIDE>::THREADS, 1)
           if (it >= C::STAGES) ok = mbar_wait(&empty_bar[s], ((it / C::STAGES) & 1) ^ 1, kGv4SiteEmpty);
           if (ok) mbar_arrive_expect_tx(&full_bar[s], stage_tx);
         }
-        if (!__shfl_sync(0x7u, ok, 0)) break;
+        if (!__shfl_sync(mask, ok, 0)) break;
         const int rb = (int)blockIdx.x + (it / n_stages) * (int)gridDim.x, st = it % n_stages;
         uint8_t* base = smem + s * C::STAGE_BYTES;
-        if (lane == 0) tma_load_3d(base, &tm_wgt, 0, rb * C::ROWS, st * C::W_BLK, &full_bar[s]);
-        else if (lane == 1) tma_load_3d(base + C::W_BYTES, &tm_act, 0, 0, st * C::A_BLK, &full_bar[s]);
-        else if (!DOTS && !TW) tma_load_2d(base + C::W_BYTES + C::A_BYTES, &tm_scale, st * C::GPS, 0, &full_bar[s]);
+        if (b2d) {
+          if (kind == 0)
+            tma_load_2d(base + blk * (C::ROWS * 128), &tm_wgt, (st * C::W_BLK + blk) * 128, rb * C::ROWS, &full_bar[s]);
+          else if (kind == 1)
+            tma_load_2d(base + C::W_BYTES + blk * (C::TOK * 128), &tm_act, (st * C::A_BLK + blk) * 128, 0,
+                        &full_bar[s]);
+          else if (!DOTS && !TW)
+            tma_load_2d(base + C::W_BYTES + C::A_BYTES, &tm_scale, st * C::GPS, 0, &full_bar[s]);
+        } else {
+          if (lane == 0) tma_load_3d(base, &tm_wgt, 0, rb * C::ROWS, st * C::W_BLK, &full_bar[s]);
+          else if (lane == 1) tma_load_3d(base + C::W_BYTES, &tm_act, 0, 0, st * C::A_BLK, &full_bar[s]);
+          else if (!DOTS && !TW) tma_load_2d(base + C::W_BYTES + C::A_BYTES, &tm_scale, st * C::GPS, 0, &full_bar[s]);
+        }
         ++issued;
       }
       // Never leave the CTA with bulk copies still landing in shared memory.
@@ -417,8 +438,9 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI, WIDE>::THREADS, 1)
     for (int j = 0; j < C::GPQ; ++j) {
       ow0[j] = swizzled_offset<W>(q * C::GPQ + j, t, r * 16 + gid, C::ROWS);
       ow1[j] = swizzled_offset<W>(q * C::GPQ + j, t, r * 16 + 8 + gid, C::ROWS);
-      oa_lo[j] = swizzled_offset<A>(q * C::GPQ + j, t, gid, Mb);
-      oa_hi[j] = swizzled_offset<A>(q * C::GPQ + j, t, gid + 8, Mb);
+      const int a_box_rows = p.gemv_boxes2d ? C::TOK : Mb;  // token box height
+      oa_lo[j] = swizzled_offset<A>(q * C::GPQ + j, t, gid, a_box_rows);
+      oa_hi[j] = swizzled_offset<A>(q * C::GPQ + j, t, gid + 8, a_box_rows);
     }
     for (int it = 0; it < total; ++it) {
       const int s = it % C::STAGES, d = it % C::DSTAGES;

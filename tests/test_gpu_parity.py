@@ -232,7 +232,10 @@ DECODE_SHAPES = [
     (1, 1536, 200),   # whole-stage boxes, partial last stage, ragged N
     (5, 3072, 4800),  # whole-stage boxes, more 32-row blocks than SMs (persistent loop)
     (16, 512, 96),    # whole-stage boxes, half a stage: K-lanes 2 and 3 see only padding
-    (3, 448, 72),     # packed rows not a multiple of 128 bytes: 2-D boxes
+    (3, 448, 72),     # packed rows not a multiple of 128 bytes: one 2-D box per block, 2048-K stage
+    (9, 1088, 200),   # 2-D boxes, 16-token tile, partial last block of every row
+    (4, 2240, 64),    # 2-D boxes, 2048-K stages (the second one partial)
+    (1, 11008, 136),  # the Llama down-projection K: 2-bit rows are 2,752 bytes
     (24, 4096, 136),  # 17..32 tokens
     (32, 1024, 64),
 ]

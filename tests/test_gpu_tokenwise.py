@@ -167,9 +167,10 @@ def test_tokenwise_rejects_bad_arguments(ops):
 def test_tokenwise_decode_sizes(ops, w, m):
     """M <= 16 runs the weight-streaming kernel in its tokenwise mode: fp32 outputs
     bit-exact against the oracle, with and without bias, ragged N and a partial
-    last K stage (K = 1536)."""
+    last K stage (K = 1536) and packed rows that are not whole
+    128-byte blocks (K = 1088)."""
     torch.manual_seed(w * 100 + m)
-    for k, n, with_bias in ((4096, 4096, True), (1536, 200, False)):
+    for k, n, with_bias in ((4096, 4096, True), (1536, 200, False), (1088, 136, True)):
         x = torch.randn(m, k, device=DEV, dtype=torch.bfloat16)
         lo, hi = {4: (-8, 8), 8: (-128, 128), 2: (-2, 2)}[w]
         codes = torch.randint(lo, hi, (n, k), device=DEV, dtype=torch.int8)
