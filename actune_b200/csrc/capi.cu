@@ -182,11 +182,12 @@ int pick_bn(int variant, int64_t M, int64_t N, int num_sms) {
 }
 
 template <int W, int A>
-cudaError_t dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, cudaStream_t s) {
+cudaError_t dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, cudaStream_t s,
+                        bool pdl = false) {
   switch (bn) {
-    case 32: return launch_group64_gemm<W, A, 32>(ta, tw, p, s);
-    case 64: return launch_group64_gemm<W, A, 64>(ta, tw, p, s);
-    default: return launch_group64_gemm<W, A, 128>(ta, tw, p, s);
+    case 32: return launch_group64_gemm<W, A, 32>(ta, tw, p, s, pdl);
+    case 64: return launch_group64_gemm<W, A, 64>(ta, tw, p, s, pdl);
+    default: return launch_group64_gemm<W, A, 128>(ta, tw, p, s, pdl);
   }
 }
 
@@ -244,9 +245,10 @@ cudaError_t dispatch_persistent(int W, int A, bool tw_mode, int bn, const CUtens
 }
 
 cudaError_t dispatch_gemm(int W, int A, int bn, bool x2, const CUtensorMap& ta, const CUtensorMap& tw,
-                          const GemmParams& p, cudaStream_t s) {
+                          const GemmParams& p, cudaStream_t s, bool pdl = false) {
 #define ACTUNE_CASE(WW, AA) \
-  if (W == WW && A == AA) return x2 ? dispatch_bn_x2<WW, AA>(bn, ta, tw, p, s) : dispatch_bn<WW, AA>(bn, ta, tw, p, s);
+  if (W == WW && A == AA)   \
+    return x2 ? dispatch_bn_x2<WW, AA>(bn, ta, tw, p, s) : dispatch_bn<WW, AA>(bn, ta, tw, p, s, pdl);
   ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
   ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
   ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
@@ -347,6 +349,30 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
     rc = encode_map(&to, out, M, N * 2, 128, 128, Swz::B128);
     if (rc != ACTUNE_OK) return rc;
     return cuda_status(dispatch_persistent(W, A, false, bn, ta, tw, to, p, g_devices[dev].num_sms, stream));
+  }
+  // AUTO with 128-column tiles whose last wave is partial: the whole waves as one
+  // launch and the remaining columns as narrower tiles in a second launch that may
+  // start while the first drains (programmatic dependent launch), so that the
+  // partial wave is shorter.  Same arithmetic per element: bit-identical output.
+  if (variant == ACTUNE_VARIANT_AUTO && !wt && dots == nullptr && bn == 128) {
+    const int sms = g_devices[dev].num_sms;
+    const int64_t mt = (M + 127) / 128, tiles = mt * ((N + 127) / 128);
+    const int64_t na = (tiles - tiles % sms) / mt;  // 128-column tiles of the whole waves
+    if (tiles > sms && tiles % sms != 0 && na > 0 && na * 128 < N) {
+      const int64_t rest = N - na * 128;
+      const int bn_b = mt * ((rest + 31) / 32) <= sms ? 32 : (mt * ((rest + 63) / 64) <= sms ? 64 : 0);
+      if (bn_b > 0) {
+        CUtensorMap tw_b;
+        rc = encode_map(&tw_b, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn_b, W == 8 ? Swz::B128 : Swz::None);
+        if (rc != ACTUNE_OK) return rc;
+        GemmParams pa = p, pb = p;
+        pa.n_end = (int)(na * 128);
+        pb.n_base = (int)(na * 128);
+        cudaError_t e = dispatch_gemm(W, A, 128, false, ta, tw, pa, stream);
+        if (e == cudaSuccess) e = dispatch_gemm(W, A, bn_b, false, ta, tw_b, pb, stream, true);
+        return cuda_status(e);
+      }
+    }
   }
   // The debug dots export always runs the one-CTA-per-SM form.
   const bool x2 = is_x2_variant(variant) && dots == nullptr;

@@ -42,6 +42,7 @@ struct GemmParams {
   int out_vec_ok;          // N % 8 == 0 and out 16-byte aligned
   int rowwise_order;       // row-scaled modes: 0 (acc*as)*ws, 1 acc*(as*ws) (the per-row A4 native order)
   int gemv_boxes2d;        // decode: packed rows not whole 128-byte blocks, one 2-D box per block
+  int n_base, n_end;       // GEMM: output columns [n_base, n_end) of [0, N) (n_end 0: N)
 };
 
 // Wait-site identifiers recorded with a device timeout.
@@ -218,7 +219,10 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
   const int G = p.G;
   const int n_iters = (G + 1) >> 1;
   const int m0 = blockIdx.x * C::BM;
-  const int n0 = blockIdx.y * BN;
+  const int n0 = p.n_base + blockIdx.y * BN;
+  // A launch that covers part of the columns lets the launch for the rest (made with
+  // programmatic stream serialization) start as soon as SMs come free.
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -582,12 +586,17 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  // Launched early after another part of the same GEMM: finish only after it, so that
+  // the stream's next operation sees both (returns at once without such a launch).
+  if (threadIdx.x == 0) griddep_wait();
 }
 
-// Host-side launch (defined per W in gemm_w*.cu).
+// Host-side launch (defined per W in gemm_w*.cu).  `pdl`: launch with programmatic
+// stream serialization (the previous kernel in the stream must be the launch of
+// another column range of the same GEMM).
 template <int W, int A, int BN>
 cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
-                                cudaStream_t stream);
+                                cudaStream_t stream, bool pdl = false);
 // The same GEMM at two CTAs per SM (Group64Cfg OCC = 2).
 template <int W, int A, int BN>
 cudaError_t launch_group64_gemm_x2(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,

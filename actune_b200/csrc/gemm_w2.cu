@@ -5,7 +5,7 @@ namespace actune {
 
 template <int W, int A, int BN>
 cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, bool pdl) {
   using C = Group64Cfg<W, A, BN>;
   const bool dots = p.dots != nullptr;
   auto kernel = dots ? group64_gemm_kernel<W, A, BN, true> : group64_gemm_kernel<W, A, BN, false>;
@@ -18,9 +18,23 @@ cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm
     if (e != cudaSuccess) return e;
     configured[dots][dev] = true;
   }
-  const dim3 grid((p.M + C::BM - 1) / C::BM, (p.N + BN - 1) / BN);
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
-  return cudaGetLastError();
+  const int n_end = p.n_end > 0 ? p.n_end : p.N;
+  const dim3 grid((p.M + C::BM - 1) / C::BM, (n_end - p.n_base + BN - 1) / BN);
+  if (!pdl) {
+    kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, tm_act, tm_wgt, p);
 }
 
 // Two CTAs per SM (no debug-dots form: the one-CTA kernel exports dots).
@@ -108,7 +122,7 @@ ACTUNE_PERSIST(8, 128, true)
 
 #define ACTUNE_INST(A, BN)                                                                                  \
   template cudaError_t launch_group64_gemm<2, A, BN>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, \
-                                                     cudaStream_t);                                            \
+                                                     cudaStream_t, bool);                                            \
   template cudaError_t launch_group64_gemm_x2<2, A, BN>(const CUtensorMap&, const CUtensorMap&,                   \
                                                         const GemmParams&, cudaStream_t);
 ACTUNE_INST(2, 32)

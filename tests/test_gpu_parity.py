@@ -198,6 +198,27 @@ def test_gemm_two_ctas_per_sm_variants(ops, w, a, variant):
     assert torch.equal(d, ops.packed_linear_dots(pa, pw, k, w, a, variant=3))
 
 
+@pytest.mark.parametrize("w,a", [(4, 8), (8, 8), (2, 2), (4, 4)])
+@pytest.mark.parametrize("m,k,n", [(600, 256, 12288), (600, 192, 3990), (600, 128, 4096)])
+def test_gemm_auto_split_waves(ops, w, a, m, k, n):
+    """AUTO splits a GEMM whose 128-column tiles leave a partial last wave into a
+    launch for the whole waves and a second, programmatically dependent launch of
+    narrower tiles for the remaining columns (BN=64 for the first shape, BN=32 for the
+    others, a ragged tail for N=3990): identical to the unsplit kernel, and sampled
+    rows bit-exact against the oracle."""
+    rows = [0, 127, 128, 599]
+    y, ref, (pa, pw, pa_h) = _case(ops, m, k, n, w, a, seed=m + k + n + w, out_dtype=torch.float32, rows=rows)
+    assert_bits(y.numpy(), ref, f"fp32 output m={m} k={k} n={n}")
+    x = inputs(m, k, m + k + n + w).to(DEV)
+    wt = weight(n, k, m + k + n + w).to(DEV)
+    codes, ws = ops.weight_codes(wt, w, a)
+    pw = ops.pack_rows(codes, w)
+    pa, as_ = ops.quantize_group64(x, a)
+    auto = ops.packed_linear(pa, as_, pw, ws, None, k, w, a, out_dtype=torch.bfloat16, variant=0)
+    whole = ops.packed_linear(pa, as_, pw, ws, None, k, w, a, out_dtype=torch.bfloat16, variant=3)
+    assert torch.equal(auto, whole)
+
+
 @pytest.mark.parametrize("w,a", PAIRS)
 @pytest.mark.parametrize("variant", [12, 13])
 def test_gemm_persistent_variants(ops, w, a, variant):
