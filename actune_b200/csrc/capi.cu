@@ -244,6 +244,21 @@ cudaError_t dispatch_persistent(int W, int A, bool tw_mode, int bn, const CUtens
   return cudaErrorInvalidValue;
 }
 
+// Wave-tail split of an AUTO GEMM with 128-column tiles: when the tiles leave a
+// partial last wave, the whole waves take the first *na128 * 128 columns and the rest
+// runs as narrower tiles (the returned width, 32 or 64, whichever fits one wave) in a
+// second launch that may start while the first drains.  0: no split.
+int wave_tail_split(int64_t M, int64_t N, int sms, int64_t* na128) {
+  const int64_t mt = (M + 127) / 128, tiles = mt * ((N + 127) / 128);
+  const int64_t na = (tiles - tiles % sms) / mt;
+  if (tiles <= sms || tiles % sms == 0 || na <= 0 || na * 128 >= N) return 0;
+  const int64_t rest = N - na * 128;
+  *na128 = na;
+  if (mt * ((rest + 31) / 32) <= sms) return 32;
+  if (mt * ((rest + 63) / 64) <= sms) return 64;
+  return 0;
+}
+
 cudaError_t dispatch_gemm(int W, int A, int bn, bool x2, const CUtensorMap& ta, const CUtensorMap& tw,
                           const GemmParams& p, cudaStream_t s, bool pdl = false) {
 #define ACTUNE_CASE(WW, AA) \
@@ -355,12 +370,9 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   // start while the first drains (programmatic dependent launch), so that the
   // partial wave is shorter.  Same arithmetic per element: bit-identical output.
   if (variant == ACTUNE_VARIANT_AUTO && !wt && dots == nullptr && bn == 128) {
-    const int sms = g_devices[dev].num_sms;
-    const int64_t mt = (M + 127) / 128, tiles = mt * ((N + 127) / 128);
-    const int64_t na = (tiles - tiles % sms) / mt;  // 128-column tiles of the whole waves
-    if (tiles > sms && tiles % sms != 0 && na > 0 && na * 128 < N) {
-      const int64_t rest = N - na * 128;
-      const int bn_b = mt * ((rest + 31) / 32) <= sms ? 32 : (mt * ((rest + 63) / 64) <= sms ? 64 : 0);
+    int64_t na = 0;
+    const int bn_b = wave_tail_split(M, N, g_devices[dev].num_sms, &na);
+    {
       if (bn_b > 0) {
         CUtensorMap tw_b;
         rc = encode_map(&tw_b, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn_b, W == 8 ? Swz::B128 : Swz::None);
@@ -436,16 +448,33 @@ int run_rowwise(const uint8_t* a, int A, const float* a_scale, const uint8_t* w,
     if (rc != ACTUNE_OK) return rc;
     return cuda_status(dispatch_persistent(W, A, true, bn, ta, tw, to, p, g_devices[dev].num_sms, stream));
   }
-  cudaError_t e = cudaErrorInvalidValue;
-#define ACTUNE_TW(WW, AA)                                                              \
-  if (W == WW && A == AA) {                                                            \
-    e = bn == 32   ? launch_group64_tokenwise<WW, AA, 32>(ta, tw, p, stream)           \
-        : bn == 64 ? launch_group64_tokenwise<WW, AA, 64>(ta, tw, p, stream)           \
-                   : launch_group64_tokenwise<WW, AA, 128>(ta, tw, p, stream);         \
-  }
-  ACTUNE_TW(2, 8) ACTUNE_TW(4, 8) ACTUNE_TW(8, 8) ACTUNE_TW(2, 4) ACTUNE_TW(4, 4) ACTUNE_TW(8, 4)
+  auto launch = [&](int bnx, const CUtensorMap& twx, const GemmParams& px, bool pdl) -> cudaError_t {
+#define ACTUNE_TW(WW, AA)                                                                      \
+  if (W == WW && A == AA)                                                                      \
+    return bnx == 32   ? launch_group64_tokenwise<WW, AA, 32>(ta, twx, px, stream, pdl)        \
+           : bnx == 64 ? launch_group64_tokenwise<WW, AA, 64>(ta, twx, px, stream, pdl)        \
+                       : launch_group64_tokenwise<WW, AA, 128>(ta, twx, px, stream, pdl);
+    ACTUNE_TW(2, 8) ACTUNE_TW(4, 8) ACTUNE_TW(8, 8) ACTUNE_TW(2, 4) ACTUNE_TW(4, 4) ACTUNE_TW(8, 4)
 #undef ACTUNE_TW
-  return cuda_status(e);
+    return cudaErrorInvalidValue;
+  };
+  if (variant == ACTUNE_VARIANT_AUTO && bn == 128) {
+    // The wave-tail split of the group-64 GEMM (bit-identical outputs).
+    int64_t na = 0;
+    const int bn_b = wave_tail_split(M, N, g_devices[dev].num_sms, &na);
+    if (bn_b > 0) {
+      CUtensorMap tw_b;
+      rc = encode_map(&tw_b, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn_b, W == 8 ? Swz::B128 : Swz::None);
+      if (rc != ACTUNE_OK) return rc;
+      GemmParams pa = p, pb = p;
+      pa.n_end = (int)(na * 128);
+      pb.n_base = (int)(na * 128);
+      cudaError_t e = launch(128, tw, pa, false);
+      if (e == cudaSuccess) e = launch(bn_b, tw_b, pb, true);
+      return cuda_status(e);
+    }
+  }
+  return cuda_status(launch(bn, tw, p, false));
 }
 
 }  // namespace

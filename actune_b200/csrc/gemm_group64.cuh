@@ -610,6 +610,6 @@ cudaError_t launch_group64_persistent(const CUtensorMap& tm_act, const CUtensorM
 // Row-scaled mode (per-token act_scale [M]; A = 8 tokenwise, A = 4 per-row A4).
 template <int W, int A, int BN>
 cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
-                                     cudaStream_t stream);
+                                     cudaStream_t stream, bool pdl = false);
 
 }  // namespace actune

@@ -60,7 +60,7 @@ cudaError_t launch_group64_gemm_x2(const CUtensorMap& tm_act, const CUtensorMap&
 
 template <int W, int A, int BN>
 cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
-                                     cudaStream_t stream) {
+                                     cudaStream_t stream, bool pdl) {
   using C = Group64Cfg<W, A, BN>;
   auto kernel = group64_gemm_kernel<W, A, BN, false, true>;
   int dev = 0;
@@ -72,17 +72,31 @@ cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMa
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  const dim3 grid((p.M + C::BM - 1) / C::BM, (p.N + BN - 1) / BN);
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
-  return cudaGetLastError();
+  const int n_end = p.n_end > 0 ? p.n_end : p.N;
+  const dim3 grid((p.M + C::BM - 1) / C::BM, (n_end - p.n_base + BN - 1) / BN);
+  if (!pdl) {
+    kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, tm_act, tm_wgt, p);
 }
 
-template cudaError_t launch_group64_tokenwise<4, 4, 32>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-template cudaError_t launch_group64_tokenwise<4, 4, 64>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-template cudaError_t launch_group64_tokenwise<4, 4, 128>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-template cudaError_t launch_group64_tokenwise<4, 8, 32>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-template cudaError_t launch_group64_tokenwise<4, 8, 64>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-template cudaError_t launch_group64_tokenwise<4, 8, 128>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+template cudaError_t launch_group64_tokenwise<4, 4, 32>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t, bool);
+template cudaError_t launch_group64_tokenwise<4, 4, 64>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t, bool);
+template cudaError_t launch_group64_tokenwise<4, 4, 128>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t, bool);
+template cudaError_t launch_group64_tokenwise<4, 8, 32>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t, bool);
+template cudaError_t launch_group64_tokenwise<4, 8, 64>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t, bool);
+template cudaError_t launch_group64_tokenwise<4, 8, 128>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t, bool);
 
 template <int W, int A, int BN, bool TW>
 cudaError_t launch_group64_persistent(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const CUtensorMap& tm_out,

@@ -181,3 +181,22 @@ def test_tokenwise_decode_sizes(ops, w, m):
         ref = O.tokenwise_linear(act.cpu().numpy(), scale.cpu().numpy(), codes.cpu().numpy(), ws.cpu().numpy(),
                                  None if bias is None else bias.float().cpu().numpy(), fma=True)
         assert bits_equal(y.cpu().numpy(), ref), (k, n)
+
+
+@pytest.mark.parametrize("w", [4, 8, 2])
+@pytest.mark.parametrize("n", [4096, 3990])
+def test_tokenwise_auto_split_waves(ops, w, n):
+    """At M=600 the 128-column tiles leave a partial last wave: AUTO runs the rest of
+    the columns as a dependent launch of narrower tiles, identical to the one-launch
+    BN128 kernel."""
+    torch.manual_seed(n + w)
+    m, k = 600, 256
+    x = torch.randn(m, k, device=DEV, dtype=torch.bfloat16)
+    lo, hi = {4: (-8, 8), 8: (-128, 128), 2: (-2, 2)}[w]
+    rows = ops.pack_rows(torch.randint(lo, hi, (n, k), device=DEV, dtype=torch.int8), w)
+    ws = torch.rand(n, device=DEV) * 0.01
+    bias = (torch.randn(n, device=DEV) * 0.1).bfloat16()
+    act, scale = ops.quantize_rows_a8(x)
+    auto = ops.tokenwise_linear(act, scale, rows, ws, bias, k, w, variant=0)
+    whole = ops.tokenwise_linear(act, scale, rows, ws, bias, k, w, variant=3)
+    assert torch.equal(auto, whole)
