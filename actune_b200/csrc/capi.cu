@@ -372,18 +372,16 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   if (variant == ACTUNE_VARIANT_AUTO && !wt && dots == nullptr && bn == 128) {
     int64_t na = 0;
     const int bn_b = wave_tail_split(M, N, g_devices[dev].num_sms, &na);
-    {
-      if (bn_b > 0) {
-        CUtensorMap tw_b;
-        rc = encode_map(&tw_b, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn_b, W == 8 ? Swz::B128 : Swz::None);
-        if (rc != ACTUNE_OK) return rc;
-        GemmParams pa = p, pb = p;
-        pa.n_end = (int)(na * 128);
-        pb.n_base = (int)(na * 128);
-        cudaError_t e = dispatch_gemm(W, A, 128, false, ta, tw, pa, stream);
-        if (e == cudaSuccess) e = dispatch_gemm(W, A, bn_b, false, ta, tw_b, pb, stream, true);
-        return cuda_status(e);
-      }
+    if (bn_b > 0) {
+      CUtensorMap tw_b;
+      rc = encode_map(&tw_b, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn_b, W == 8 ? Swz::B128 : Swz::None);
+      if (rc != ACTUNE_OK) return rc;
+      GemmParams pa = p, pb = p;
+      pa.n_end = (int)(na * 128);
+      pb.n_base = (int)(na * 128);
+      cudaError_t e = dispatch_gemm(W, A, 128, false, ta, tw, pa, stream);
+      if (e == cudaSuccess) e = dispatch_gemm(W, A, bn_b, false, ta, tw_b, pb, stream, true);
+      return cuda_status(e);
     }
   }
   // The debug dots export always runs the one-CTA-per-SM form.
