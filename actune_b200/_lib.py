@@ -10,11 +10,7 @@ import ctypes
 import threading
 from pathlib import Path
 
-import os
-
-# ACTUNE_B200_LIB may point at another build of the same library (for example
-# one compiled with different ACTUNE_B200_DEFINES); default is the in-tree build.
-LIB_PATH = Path(os.environ.get("ACTUNE_B200_LIB") or Path(__file__).resolve().with_name("libactune_b200.so"))
+LIB_PATH = Path(__file__).resolve().with_name("libactune_b200.so")
 
 OK = 0
 ERR_INVALID_VALUE = 1

@@ -21,9 +21,6 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 BUILD = PKG / "_build"
 LIB = PKG / "libactune_b200.so"
-# Optional extra nvcc defines and output path, for building experimental
-# variants side by side (e.g. ACTUNE_B200_DEFINES="-DACTUNE_PREBIAS=1").
-EXTRA_DEFINES = os.environ.get("ACTUNE_B200_DEFINES", "").split()
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-rdc=true", "-Xcompiler", "-fPIC,-O2",
@@ -61,7 +58,7 @@ def build(force: bool = False, verbose_ptxas: bool = False, jobs: int | None = N
 
     def compile_one(so):
         s, o = so
-        cmd = [cc, *ARCH, *NVCC_FLAGS, *EXTRA_DEFINES, "-I", str(INCLUDE), "-c", str(s), "-o", str(o)]
+        cmd = [cc, *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(s), "-o", str(o)]
         if verbose_ptxas:
             cmd += ["-Xptxas", "-v"]
         r = subprocess.run(cmd, capture_output=True, text=True)

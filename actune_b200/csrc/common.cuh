@@ -13,11 +13,32 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "actune_b200 kernels are written for sm_100a (Blackwell) only"
 #endif
 
 namespace actune {
+
+// Raises `Kernel`'s dynamic shared-memory limit to `bytes` on the current device,
+// once per device.  Safe for concurrent first calls from several host threads
+// (std::call_once per device); devices beyond the first kMaxDevices ordinals are
+// refused with cudaErrorInvalidDevice rather than left unconfigured.
+constexpr int kMaxDevices = 64;
+template <auto Kernel>
+cudaError_t ensure_smem_limit(int bytes) {
+  static std::once_flag once[kMaxDevices];
+  static cudaError_t status[kMaxDevices];
+  int dev = 0;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::call_once(once[dev], [&] {
+    status[dev] = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  });
+  return status[dev];
+}
 
 // ---------------------------------------------------------------------------
 // Device error word (first error wins).  Codes are the ACTUNE_DEV_* values in

@@ -505,9 +505,36 @@ __global__ void __launch_bounds__(WtCfg<W, A, BT>::THREADS, 1)
   }
 }
 
-// Host-side launch (defined per W in gemm_wt_w*.cu).
+// Host-side launch (instantiated per W in gemm_wt_w*.cu with ACTUNE_INSTANTIATE_WT(W)).
 template <int W, int A, int BT>
 cudaError_t launch_wt_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
                            cudaStream_t stream);
 
+#ifdef ACTUNE_WT_LAUNCH_DEFINITIONS
+template <int W, int A, int BT>
+cudaError_t launch_wt_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
+                           cudaStream_t stream) {
+  using C = WtCfg<W, A, BT>;
+  const bool dots = p.dots != nullptr;
+  constexpr auto k_dots = wt_gemm_kernel<W, A, BT, true>;
+  constexpr auto k_out = wt_gemm_kernel<W, A, BT, false>;
+  const cudaError_t e = dots ? ensure_smem_limit<k_dots>(C::SMEM_BYTES) : ensure_smem_limit<k_out>(C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  auto kernel = dots ? k_dots : k_out;
+  const dim3 grid((p.M + BT - 1) / BT, (p.N + C::BM - 1) / C::BM);
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
+  return cudaGetLastError();
+}
+#endif
+
 }  // namespace actune
+
+// All token tiles (16, 32, 64, 128) for A in {2, 4, 8} at weight width W.
+#define ACTUNE_WT_INST(W, A, BT) \
+  template cudaError_t launch_wt_gemm<W, A, BT>(const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+#define ACTUNE_INSTANTIATE_WT(W)                                                                             \
+  namespace actune {                                                                                         \
+  ACTUNE_WT_INST(W, 2, 16) ACTUNE_WT_INST(W, 2, 32) ACTUNE_WT_INST(W, 2, 64) ACTUNE_WT_INST(W, 2, 128)       \
+  ACTUNE_WT_INST(W, 4, 16) ACTUNE_WT_INST(W, 4, 32) ACTUNE_WT_INST(W, 4, 64) ACTUNE_WT_INST(W, 4, 128)       \
+  ACTUNE_WT_INST(W, 8, 16) ACTUNE_WT_INST(W, 8, 32) ACTUNE_WT_INST(W, 8, 64) ACTUNE_WT_INST(W, 8, 128)       \
+  }

@@ -605,22 +605,23 @@ static cudaError_t launch_gemv4_hi(const CUtensorMap& ta, const CUtensorMap& tw,
   using C = Gemv4Cfg<W, A, HI, WIDE>;
   const bool dots = !TW && p.dots != nullptr;
   void (*kernel)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
+  cudaError_t e;
   if constexpr (WIDE) {
     if (dots) return cudaErrorInvalidValue;  // the dots export runs 1024-K stages
-    kernel = gemv4_group64_kernel<W, A, HI, false, TW, true>;
+    constexpr auto k = gemv4_group64_kernel<W, A, HI, false, TW, true>;
+    kernel = k;
+    e = ensure_smem_limit<k>(C::SMEM_BYTES);
+  } else if constexpr (TW) {
+    constexpr auto k = gemv4_group64_kernel<W, A, HI, false, TW>;
+    kernel = k;
+    e = ensure_smem_limit<k>(C::SMEM_BYTES);
   } else {
-    kernel = TW ? gemv4_group64_kernel<W, A, HI, false, TW>
-                : (dots ? gemv4_group64_kernel<W, A, HI, true> : gemv4_group64_kernel<W, A, HI, false>);
+    constexpr auto k_dots = gemv4_group64_kernel<W, A, HI, true>;
+    constexpr auto k_out = gemv4_group64_kernel<W, A, HI, false>;
+    kernel = dots ? k_dots : k_out;
+    e = dots ? ensure_smem_limit<k_dots>(C::SMEM_BYTES) : ensure_smem_limit<k_out>(C::SMEM_BYTES);
   }
-  int dev = 0;
-  cudaGetDevice(&dev);
-  static bool configured[2][64] = {};
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dots][dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    configured[dots][dev] = true;
-  }
+  if (e != cudaSuccess) return e;
   const int blocks = (p.N + C::ROWS - 1) / C::ROWS;
   const int grid = blocks < num_sms ? blocks : num_sms;
   kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, ts, p);
@@ -650,16 +651,11 @@ static cudaError_t launch_gemv_t(const CUtensorMap& ta, const CUtensorMap& tw, c
                                  cudaStream_t stream) {
   using C = GemvCfg<W, A, MT>;
   const bool dots = p.dots != nullptr;
-  auto kernel = dots ? gemv_group64_kernel<W, A, MT, true> : gemv_group64_kernel<W, A, MT, false>;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  static bool configured[2][64] = {};
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dots][dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    configured[dots][dev] = true;
-  }
+  constexpr auto k_dots = gemv_group64_kernel<W, A, MT, true>;
+  constexpr auto k_out = gemv_group64_kernel<W, A, MT, false>;
+  const cudaError_t e = dots ? ensure_smem_limit<k_dots>(C::SMEM_BYTES) : ensure_smem_limit<k_out>(C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  auto kernel = dots ? k_dots : k_out;
   kernel<<<(p.N + C::ROWS - 1) / C::ROWS, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, p);
   return cudaGetLastError();
 }

@@ -8,36 +8,26 @@
 // the middle of an episode).  For them this entry point keeps the activation
 // scratch -- packed codes and group scales of one call -- in a fixed array in
 // this library's device memory, so the caller passes only inputs and outputs.
-#include <mutex>
-
 #include "actune_b200.h"
 #include "kernels.cuh"
 
 // The scratch itself.  In host code `g_noalloc_scratch` is only a stand-in
-// symbol, not a device address: the device address is obtained once per device
-// with cudaGetSymbolAddress below.  Every device that loads this library holds
-// these bytes until the process exits.
+// symbol, not a device address: the device address is looked up with
+// cudaGetSymbolAddress below, with the device current.  Every device that loads
+// this library holds these bytes until the process exits.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[ACTUNE_NOALLOC_SCRATCH_BYTES];
 
 namespace {
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mutex;
-void* g_scratch_address[kMaxDevices] = {};
-
-// Device address of g_noalloc_scratch on the current device (looked up on the
-// first call per device, with that device current).
+// Device address of g_noalloc_scratch on the current device.  Looked up on every
+// call (a table lookup once the library's module is loaded on the device), so a
+// context that was reset and re-created gets the array's new address instead of
+// a stale one.  The first call on a device also loads the module there, which is
+// why that first call must come before any stream capture.
 int scratch_address(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return ACTUNE_ERR_CUDA;
-  if (dev < 0 || dev >= kMaxDevices) return ACTUNE_ERR_DEVICE;
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_address[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return ACTUNE_ERR_CUDA;
-    g_scratch_address[dev] = p;
-  }
-  *out = g_scratch_address[dev];
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return ACTUNE_ERR_CUDA;
+  *out = p;
   return ACTUNE_OK;
 }
 

@@ -20,7 +20,6 @@ the gated activation use the glue kernels of include/actune_b200_harness.h.
 from __future__ import annotations
 
 import ctypes
-import math
 
 import torch
 import torch.nn.functional as F
@@ -244,4 +243,3 @@ def config_cycle():
 
 
 assert set(config_cycle()) == set(CONFIGURATIONS)
-_ = math  # keep import (rope tables use torch math)

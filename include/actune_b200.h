@@ -184,9 +184,11 @@ int actune_grouped_linear(const void* x, int x_dtype, int64_t M, int64_t K, cons
  * ACTUNE_NOALLOC_SCRATCH_BYTES (8 MiB) in this library's device memory, held on
  * every device that loads the library until the process exits.  Requests with
  * actune_grouped_linear_workspace_size(M, K, A) above that size return
- * ACTUNE_ERR_WORKSPACE without launching.  The first call on a device looks up
- * the array's device address (cudaGetSymbolAddress) with that device current;
- * make that first call before any stream capture.  The function allocates
+ * ACTUNE_ERR_WORKSPACE without launching.  Every call looks up the array's
+ * device address (cudaGetSymbolAddress) with the device current, so it stays
+ * valid across a device reset; the first call on a device also loads this
+ * library's device code there, so make that first call before any stream
+ * capture.  The function allocates
  * nothing.  All calls share the one array and it keeps the last call's contents
  * (no part of it needs to start at zero): calls that overlap on the GPU (other
  * streams, other threads) race on it and must be serialised by the caller. */

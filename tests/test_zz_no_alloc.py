@@ -69,3 +69,25 @@ def test_noalloc_refuses_requests_beyond_its_scratch():
     null = ctypes.c_void_p(0)
     rc = fn(null, _lib.DTYPE_BF16, m, k, null, null, null, 0, 64, 4, 8, null, _lib.DTYPE_BF16, 0, null)
     assert rc == _lib.ERR_WORKSPACE
+
+
+def test_noalloc_boundary_exactly_at_the_scratch_size():
+    """A request whose scratch is exactly the array's size runs and matches the
+    workspace entry point; one more token row is refused."""
+    from actune_b200 import _lib, ops
+    fn = _noalloc()
+    m, k, n, w, a = 7710, 1024, 256, 4, 8
+    size = _lib.lib().actune_grouped_linear_workspace_size
+    assert size(m, k, a) == NOALLOC_SCRATCH_BYTES and size(m + 1, k, a) > NOALLOC_SCRATCH_BYTES
+    x, pw, ws, bias = _inputs(300, m, k, n, w, a)
+    expected = ops.grouped_linear(x, pw, ws, bias, w, a)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = fn(_ptr(x), _lib.DTYPE_BF16, m, k, _ptr(pw), _ptr(ws), _ptr(bias), _lib.DTYPE_BF16, n, w, a,
+            _ptr(out), _lib.DTYPE_BF16, _lib.VARIANT_AUTO, stream)
+    torch.cuda.synchronize()
+    assert rc == _lib.OK, _lib.status_string(rc)
+    assert torch.equal(out, expected)
+    null = ctypes.c_void_p(0)
+    rc = fn(null, _lib.DTYPE_BF16, m + 1, k, null, null, null, 0, n, w, a, null, _lib.DTYPE_BF16, 0, null)
+    assert rc == _lib.ERR_WORKSPACE
