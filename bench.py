@@ -18,7 +18,7 @@ Lines (one JSON line from rank 0):
   peak measured here with torch._int_mm, ``cpu_baseline`` = the reference's CPU
   dequantize-and-matmul formula on a bounded sample of layers.
 * ``--impl reference``: the reference's CPU formula (the oracle port) on the
-  host cores, each step a bounded sample of layers scaled to a whole chunk.
+  host cores, each step one whole chunk (all 32 layers).
 
 Multi-GPU: one process per GPU (torchrun), independent policy replicas, no
 data-path collective; ``scaling`` = weak.
@@ -58,30 +58,43 @@ def parse():
 
 
 # ---------------------------------------------------------------------------- CPU (reference formula)
+PROJ_SHAPES = {"qkv": (3 * HIDDEN, HIDDEN), "o": (HIDDEN, HIDDEN), "gu": (2 * MLP, HIDDEN), "down": (HIDDEN, MLP)}
+
+
+def cpu_layer_weights(seed):
+    """Random-init bf16 projection weights of one decoder layer, N(0, 0.02), drawn on the host."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    return {name: (torch.randn(n, k, generator=g) * 0.02).bfloat16() for name, (n, k) in PROJ_SHAPES.items()}
+
+
 class CpuLayer:
     """One decoder layer evaluated with the reference's CPU dequantize-and-matmul
     formula for every projection (reference tests/test_kernels.py:42-44:
     F.linear(activation_reference(x, a), q.float() * scale[:, None])) and fp32
-    torch ops for norms, rotary embedding and attention."""
+    torch ops for norms, rotary embedding and attention.
 
-    def __init__(self, seed):
+    `weights` maps qkv / o / gu / down to bf16 [N, K] host tensors -- the same
+    values the GPU model is built from when the two are compared."""
+
+    def __init__(self, weights, tokens=TOKENS):
         import torch
         from oracle import oracle as O
-        g = torch.Generator().manual_seed(seed)
+        self.tokens = tokens
         self.w = {}
-        for name, (n, k) in {"qkv": (3 * HIDDEN, HIDDEN), "o": (HIDDEN, HIDDEN), "gu": (2 * MLP, HIDDEN),
-                             "down": (HIDDEN, MLP)}.items():
-            wt = (torch.randn(n, k, generator=g) * 0.02).bfloat16().float()
-            codes, scale = O.weight_codes(wt.numpy(), 4, 8)
+        for name, wt in weights.items():
+            codes, scale = O.weight_codes(wt.float().numpy(), 4, 8)
             self.w[name] = O.dequant_weight(torch.from_numpy(codes), torch.from_numpy(scale))  # hoisted
         inv = 1.0 / (10000.0 ** (torch.arange(0, 128, 2, dtype=torch.float32) / 128))
-        ang = torch.arange(TOKENS, dtype=torch.float32)[:, None] * inv[None, :]
+        ang = torch.arange(tokens, dtype=torch.float32)[:, None] * inv[None, :]
         self.cos, self.sin = ang.cos(), ang.sin()
 
     def forward(self, x):
         import torch
         import torch.nn.functional as F
         from oracle import oracle as O
+
+        T = self.tokens
 
         def norm(v):
             return v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + 1e-5)
@@ -94,71 +107,77 @@ class CpuLayer:
         h = norm(x)
         qkv = O.dequant_linear(h, self.w["qkv"], None, 8)
         q, k, v = qkv.split(HIDDEN, -1)
-        q = rope(q.view(TOKENS, 32, 128)).transpose(0, 1)
-        k = rope(k.view(TOKENS, 32, 128)).transpose(0, 1)
-        v = v.view(TOKENS, 32, 128).transpose(0, 1)
-        a = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(0, 1).reshape(TOKENS, HIDDEN)
+        q = rope(q.view(T, 32, 128)).transpose(0, 1)
+        k = rope(k.view(T, 32, 128)).transpose(0, 1)
+        v = v.view(T, 32, 128).transpose(0, 1)
+        a = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(0, 1).reshape(T, HIDDEN)
         x = x + O.dequant_linear(a, self.w["o"], None, 8)
         gu = O.dequant_linear(norm(x), self.w["gu"], None, 8)
         g, u = gu.split(MLP, -1)
         return x + O.dequant_linear(F.silu(g) * u, self.w["down"], None, 8)
 
 
+def cpu_chunk(layers, x0, n_layers=LAYERS):
+    """One action chunk of the CPU formula: n_layers decoder layers, cycling `layers`."""
+    x = x0
+    for i in range(n_layers):
+        x = layers[i % len(layers)].forward(x)
+    return x
+
+
 def cpu_sample(layers_in_sample, repeats=3, warmup=1):
     """Median seconds for `layers_in_sample` layers of the CPU formula."""
     import torch
     torch.set_num_threads(os.cpu_count() or 1)
-    layers = [CpuLayer(100 + i) for i in range(layers_in_sample)]
+    layers = [CpuLayer(cpu_layer_weights(100 + i)) for i in range(min(layers_in_sample, 2))]
     x0 = torch.randn(TOKENS, HIDDEN, generator=torch.Generator().manual_seed(1)).bfloat16().float()
-
-    def run():
-        x = x0
-        for layer in layers:
-            x = layer.forward(x)
-        return x
-
     for _ in range(warmup):
-        run()
+        cpu_chunk(layers, x0, layers_in_sample)
     times = []
     for _ in range(repeats):
         t0 = time.perf_counter()
-        run()
+        cpu_chunk(layers, x0, layers_in_sample)
         times.append(time.perf_counter() - t0)
     return statistics.median(times)
 
 
+def bench_config(world):
+    """The `config` object both arms print (identical keys and values)."""
+    return {"workload": WORKLOAD, "tokens": TOKENS, "layers": LAYERS, "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (3.4 GB packed weights streamed per chunk, L2 126 MB)"}
+
+
 def reference_arm(args):
+    """The reference's CPU path (its dequantize-and-matmul formula, as the oracle port)
+    on the host cores: every step is one whole action chunk, all 32 decoder layers
+    (two weight sets cycled; each layer's ~0.8 GB of fp32 weights is far beyond the
+    CPU caches, so the cycling changes nothing about the memory traffic)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     torch.set_num_threads(os.cpu_count() or 1)
-    n = max(1, args.cpu_sample_layers // 2)
-    layers = [CpuLayer(100 + i) for i in range(n)]
+    layers = [CpuLayer(cpu_layer_weights(100 + i)) for i in range(2)]
     x0 = torch.randn(TOKENS, HIDDEN, generator=torch.Generator().manual_seed(1)).bfloat16().float()
-
-    def step():
-        x = x0
-        for layer in layers:
-            x = layer.forward(x)
-
     for _ in range(args.warmup):
-        step()
+        cpu_chunk(layers, x0, args.layers)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
-    per_step = (time.perf_counter() - t0) / args.steps
-    ms_chunk = per_step / n * LAYERS * 1e3
-    line = {"impl": "reference", "metric": METRIC, "value": round(ms_chunk, 3), "unit": "ms",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_chunk, 3),
+        cpu_chunk(layers, x0, args.layers)
+    ms_step = (time.perf_counter() - t0) / args.steps * 1e3
+    line = {"impl": "reference", "metric": METRIC, "value": round(ms_step, 3), "unit": "ms",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+            "ms_per_chunk": round(ms_step, 3), "chunks_per_step": 1,
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic (seeded random activations, random-init weights)",
-            "config": {"workload": WORKLOAD, "tokens": TOKENS, "layers": LAYERS, "parallelism": "replicas"},
-            "cpu_baseline": {"value": round(ms_chunk, 3), "unit": "ms", "cores": torch.get_num_threads(),
+            "config": bench_config(world),
+            "cpu_baseline": {"value": round(ms_step, 3), "unit": "ms", "cores": torch.get_num_threads(),
                              "kind": "port",
-                             "sample": f"{n} of {LAYERS} layers per step (oracle port of the reference's "
-                                       f"dequantize-and-matmul formula), scaled x{LAYERS / n:g} to a chunk"},
-            "e2e": {"value": round(ms_chunk, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                             "sample": f"whole chunks: {args.layers} decoder layers per step (two weight sets "
+                                       "cycled) of the reference's dequantize-and-matmul formula (oracle port), "
+                                       f"{args.steps} timed steps after {args.warmup} warm-up"},
+            "e2e": {"value": round(ms_step, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -355,9 +374,8 @@ def ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (seeded random token embeddings, random-init weights)",
-            "config": {"workload": WORKLOAD, "tokens": TOKENS, "layers": args.layers, "chunks_per_step": world,
-                       "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (3.4 GB packed weights "
-                       "streamed per step, L2 126 MB)"},
+            "ms_per_chunk": round(ms_step / world, 4), "chunks_per_step": world,
+            "config": bench_config(world),
             "e2e": {"value": round(ms_step_e2e / world, 4), "unit": "ms",
                     "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
                     "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
