@@ -45,6 +45,10 @@ EXPORTS = (
     "actune_device_error",
     "actune_abi_version",
     "actune_last_cuda_error",
+    "actune_grouped_linear_noalloc",
+    "actune_set_wait_limit_ns",
+    "actune_wait_limit_ns",
+    "actune_selftest_wait_timeout",
 )
 
 _LIB = None
@@ -79,6 +83,10 @@ def _declare(L):
     L.actune_device_error.argtypes = [ctypes.POINTER(i32), ctypes.POINTER(i32), i32]
     L.actune_abi_version.argtypes = []
     L.actune_last_cuda_error.argtypes = []
+    L.actune_grouped_linear_noalloc.argtypes = [p, i32, i64, i64, p, p, p, i32, i64, i32, i32, p, i32, i32, p]
+    L.actune_set_wait_limit_ns.argtypes = [ctypes.c_uint64]
+    L.actune_wait_limit_ns.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
+    L.actune_selftest_wait_timeout.argtypes = [i32, p]
     for name in EXPORTS:
         if name not in ("actune_status_string", "actune_grouped_linear_workspace_size"):
             getattr(L, name).restype = i32
@@ -109,6 +117,18 @@ def check(status: int, what: str = "") -> None:
         if status == ERR_CUDA:
             msg += f" [cudaError {lib().actune_last_cuda_error()}]"
         raise ActuneError(status, msg)
+
+
+def wait_limit_ns() -> int:
+    """The current device's pipeline wait limit (ns)."""
+    v = ctypes.c_uint64(0)
+    check(lib().actune_wait_limit_ns(ctypes.byref(v)), "wait_limit_ns")
+    return v.value
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Set the current device's pipeline wait limit (1 ms .. 60 s)."""
+    check(lib().actune_set_wait_limit_ns(int(ns)), "set_wait_limit_ns")
 
 
 def device_error(reset: bool = False):

@@ -1,7 +1,7 @@
 // Shared device helpers for the group-64 packed-integer path (sm_100a only).
 //
 // Everything that waits (mbarrier phases) waits with a time limit: after
-// kWaitLimitNs without progress the waiting thread records an error code in
+// g_actune_wait_limit_ns without progress the waiting thread records an error code in
 // g_actune_error and returns false, so a broken pipeline ends the kernel with
 // an error status the host can read (actune_device_error) instead of hanging
 // the GPU.
@@ -46,8 +46,12 @@ cudaError_t ensure_smem_limit(int bytes) {
 // ---------------------------------------------------------------------------
 extern __device__ int g_actune_error;
 extern __device__ int g_actune_error_site;
-
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: legitimate waits are microseconds
+// Time limit of every pipeline wait on this device (ns).  Legitimate waits are
+// microseconds; the default is 2 s, and actune_set_wait_limit_ns changes it (the
+// failure-detection self-test shortens it so that its deliberately abandoned wait
+// ends quickly).
+extern __device__ unsigned long long g_actune_wait_limit_ns;
+constexpr unsigned long long kDefaultWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ void report_error(int code, int site) {
   if (atomicCAS(&g_actune_error, 0, code) == 0) atomicExch(&g_actune_error_site, site);
@@ -112,7 +116,8 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 
 constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms per sleep; the 2 s limit is checked between sleeps
 
-// Wait for the phase with the given parity to complete; false after the limit.
+// Wait for the phase with the given parity to complete; false after the limit
+// (g_actune_wait_limit_ns, checked every 16 sleeps).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
@@ -123,7 +128,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
       const uint64_t now = globaltimer();
       if (t0 == 0) {
         t0 = now;
-      } else if (now - t0 > kWaitLimitNs) {
+      } else if (now - t0 > g_actune_wait_limit_ns) {
         report_error(1 /* ACTUNE_DEV_TIMEOUT */, site);
         return false;
       }

@@ -19,6 +19,7 @@ namespace actune {
 
 __device__ int g_actune_error = 0;
 __device__ int g_actune_error_site = 0;
+__device__ unsigned long long g_actune_wait_limit_ns = kDefaultWaitLimitNs;
 
 template <typename T>
 __device__ __forceinline__ void load8(const T* p, float (&v)[8]);

@@ -196,6 +196,23 @@ int actune_grouped_linear_noalloc(const void* x, int x_dtype, int64_t M, int64_t
                                   const float* w_scale, const void* bias, int bias_dtype, int64_t N, int W, int A,
                                   void* out, int out_dtype, int variant, void* stream);
 
+/* Failure detection (no counterpart in the reference, whose kernels have no
+ * bounded waits).  Every pipeline wait of this library's kernels gives up after a
+ * time limit, records ACTUNE_DEV_TIMEOUT and the wait site in the device error
+ * word (actune_device_error) and lets the kernel finish, so a broken pipeline
+ * never hangs the GPU and the context stays usable.
+ *
+ * actune_set_wait_limit_ns: sets that limit on the current device (default 2 s;
+ * accepted range 1 ms .. 60 s) for kernels launched afterwards.  Synchronous.
+ * actune_wait_limit_ns: reads it.
+ * actune_selftest_wait_timeout: launches a one-warp kernel that waits, with the
+ * same bounded primitive, on a barrier nothing arrives on; it records
+ * ACTUNE_DEV_TIMEOUT with `site` (> 0) once the limit passes and returns.  It
+ * holds no tensor memory and no copies in flight.  For tests of the error path. */
+int actune_set_wait_limit_ns(uint64_t ns);
+int actune_wait_limit_ns(uint64_t* ns);
+int actune_selftest_wait_timeout(int site, void* stream);
+
 /* Human-readable text for an actune_status (static storage). */
 const char* actune_status_string(int status);
 
