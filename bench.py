@@ -141,9 +141,9 @@ def cpu_sample(layers_in_sample, repeats=3, warmup=1):
     return statistics.median(times)
 
 
-def bench_config(world):
+def bench_config(world, layers=LAYERS):
     """The `config` object both arms print (identical keys and values)."""
-    return {"workload": WORKLOAD, "tokens": TOKENS, "layers": LAYERS, "parallelism": f"replicas x{world}",
+    return {"workload": WORKLOAD, "tokens": TOKENS, "layers": layers, "parallelism": f"replicas x{world}",
             "l2": "inputs larger than L2 (3.4 GB packed weights streamed per chunk, L2 126 MB)"}
 
 
@@ -171,7 +171,7 @@ def reference_arm(args):
             "ms_per_chunk": round(ms_step, 3), "chunks_per_step": 1,
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic (seeded random activations, random-init weights)",
-            "config": bench_config(world),
+            "config": bench_config(world, args.layers),
             "cpu_baseline": {"value": round(ms_step, 3), "unit": "ms", "cores": torch.get_num_threads(),
                              "kind": "port",
                              "sample": f"whole chunks: {args.layers} decoder layers per step (two weight sets "
@@ -375,7 +375,7 @@ def ours(args):
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (seeded random token embeddings, random-init weights)",
             "ms_per_chunk": round(ms_step / world, 4), "chunks_per_step": world,
-            "config": bench_config(world),
+            "config": bench_config(world, args.layers),
             "e2e": {"value": round(ms_step_e2e / world, 4), "unit": "ms",
                     "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
                     "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},

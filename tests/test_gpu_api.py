@@ -356,3 +356,46 @@ def test_small_oft_backbone_graph_vs_eager():
                 assert torch.equal(policy(x), eager[q])
         policy.release()
     assert not torch.equal(eager["q00"], eager["q11"])
+
+
+def test_graph_replay_literal_constants_and_shared_inputs():
+    """Literal CUDA constants built inside the function are made while warming up and
+    handed out as clones (the function may update them in place); graphs of several
+    precisions for one input signature share one set of static inputs."""
+    from actune_b200.graph import GraphReplay
+    from actune_b200.layers import install_bank
+    from actune_b200.precision import precision_profile
+    model = tiny_model(2)
+    runtime = install_bank(model, tiny_bank(model), {"0": {"w4a8": None, "w2a8": None},
+                                                     "2": {"w4a8": None, "w2a8": None}})
+
+    def step(x):
+        t = torch.tensor(1.0, dtype=torch.float32, device="cuda")
+        t += 0.5  # in place, as the reference's sampler updates its time tensor
+        return model(x).float() * t
+
+    x = torch.randn(4, 128, device="cuda", dtype=torch.bfloat16)
+    with torch.inference_mode():
+        eager = {q: None for q in ("q00", "q11")}
+        for q in eager:
+            with precision_profile(q):
+                eager[q] = model(x).float() * 1.5
+    replay = GraphReplay(step, runtime.modules)
+    replay.enabled = True
+    for q in ("q00", "q11", "q00", "q11"):
+        with precision_profile(q), torch.inference_mode():
+            out = replay(x.clone()).clone()
+        assert torch.equal(out, eager[q]), q
+    assert len(replay.graphs) == 2 and replay.replays == 4 and len(replay.constants) == 1
+    assert len(replay._slots) == 1  # one static input set for both precisions
+    replay.release()
+
+    def late_literal(x):
+        if torch.cuda.is_current_stream_capturing():
+            torch.tensor(2.0, device="cuda")  # first seen during capture
+        return x * 2
+
+    late = GraphReplay(late_literal, {})
+    late.enabled = True
+    with pytest.raises(RuntimeError, match="Unwarmed CUDA constant"):
+        late(torch.ones(3, device="cuda"))
