@@ -138,7 +138,13 @@ class DecoderLayer(torch.nn.Module):
         self.gate_up_proj = torch.nn.Linear(hidden, 2 * mlp, bias=False, **kw)
         self.down_proj = torch.nn.Linear(mlp, hidden, bias=False, **kw)
 
-    def forward(self, x, residual, cos, sin):
+    def forward(self, x, residual, cos, sin, past=None, store=None, causal=True):
+        """(x, residual) -> (mlp output, new residual stream), pre-norm.
+
+        `store`: (k, v) buffers [1, kv_heads, T, head_dim] that receive this call's
+        rotated keys and values (a prefix cache); `past`: such buffers from an
+        earlier call, prepended to this call's keys and values; `causal`: causal
+        attention within the call (bidirectional otherwise)."""
         T = x.shape[0]
         h, residual = rmsnorm(x, self.input_norm, self.eps, residual, self.gemma, input_bits(self.qkv_proj))
         qkv = self.qkv_proj(h)
@@ -148,7 +154,14 @@ class DecoderLayer(torch.nn.Module):
         q = q.view(T, self.heads, self.head_dim).transpose(0, 1).unsqueeze(0)
         k = k.view(T, self.kv_heads, self.head_dim).transpose(0, 1).unsqueeze(0)
         v = v.view(T, self.kv_heads, self.head_dim).transpose(0, 1).unsqueeze(0)
-        attn = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=self.kv_heads != self.heads)
+        if store is not None:
+            store[0].copy_(k)
+            store[1].copy_(v)
+        if past is not None:
+            k = torch.cat([past[0], k], dim=2)
+            v = torch.cat([past[1], v], dim=2)
+        attn = F.scaled_dot_product_attention(q, k, v, is_causal=causal and past is None,
+                                              enable_gqa=self.kv_heads != self.heads)
         attn = attn.squeeze(0).transpose(0, 1).reshape(T, self.heads * self.head_dim)
         x = self.o_proj(attn)
         h, residual = rmsnorm(x, self.post_norm, self.eps, residual, self.gemma, input_bits(self.gate_up_proj))
@@ -192,39 +205,48 @@ class OFTBackbone(torch.nn.Module):
         return a.float().reshape(self.chunk)
 
 
-def projection_names(model):
+def projection_names(model, stacks=("layers",)):
     names = []
-    for i in range(len(model.layers)):
-        for proj in ("qkv_proj", "o_proj", "gate_up_proj", "down_proj"):
-            names.append(f"layers.{i}.{proj}")
+    for stack in stacks:
+        for i in range(len(getattr(model, stack))):
+            for proj in ("qkv_proj", "o_proj", "gate_up_proj", "down_proj"):
+                names.append(f"{stack}.{i}.{proj}")
     return names
 
 
-def build_w4a8_bank(model, tokens, switchable=("layers.0.down_proj", "layers.1.down_proj")):
-    """Synthetic W4A8-average SharedBank: every projection W4A8, two binary
-    switchable matrices (W4A8 / W2A8), four distinct configurations."""
-    names = projection_names(model)
+def build_bank(model, tokens, base, alternate, switchable, stacks=("layers",)):
+    """Synthetic SharedBank: every projection in mode `base`, two binary switchable
+    matrices that take mode `alternate` in the configurations that select them
+    (q11: neither, q10: the second, q01: the first, q00: both).  `tokens` maps a
+    stack name to the token rows one request feeds its projections."""
+    names = projection_names(model, stacks)
     shapes = {n: [model.get_submodule(n).out_features, model.get_submodule(n).in_features] for n in names}
-    counts = {n: tokens * shapes[n][1] for n in names}
-    base = {n: "w4a8" for n in names}
+    counts = {n: tokens[n.split(".")[0]] * shapes[n][1] for n in names}
+    base_cfg = {n: base for n in names}
     a, b = switchable
     configurations = {
-        "q11": dict(base),
-        "q10": {**base, b: "w2a8"},
-        "q01": {**base, a: "w2a8"},
-        "q00": {**base, a: "w2a8", b: "w2a8"},
+        "q11": dict(base_cfg),
+        "q10": {**base_cfg, b: alternate},
+        "q01": {**base_cfg, a: alternate},
+        "q00": {**base_cfg, a: alternate, b: alternate},
     }
     version_bytes = {n: {m: expected_version_bytes(shapes[n][0], shapes[n][1], int(m[1]), int(m[3]))
                          for m in {c[n] for c in configurations.values()}} for n in names}
     groups = {}
     for n in names:
-        groups.setdefault(n.split(".")[-1], []).append(n)
+        groups.setdefault(n.split(".")[0] + "." + n.split(".")[-1], []).append(n)
     resident = sum(version_bytes[n][m] for n in names for m in version_bytes[n])
     bank = SharedBank(configurations=configurations, shapes=shapes, activation_elements=counts,
-                      shape_groups=list(groups.values()), version_bytes=version_bytes, budget="w4a8",
+                      shape_groups=list(groups.values()), version_bytes=version_bytes, budget=base,
                       storage_limit=resident + 1024)
     clips = {n: {m: None for m in version_bytes[n]} for n in names}
     return bank.validate(), clips
+
+
+def build_w4a8_bank(model, tokens, switchable=("layers.0.down_proj", "layers.1.down_proj")):
+    """W4A8-average bank of the OFT backbone: every projection W4A8, two binary
+    switchable matrices (W4A8 / W2A8), four distinct configurations."""
+    return build_bank(model, {"layers": tokens}, "w4a8", "w2a8", switchable)
 
 
 def make_oft_policy(layers=32, tokens=600, device="cuda", seed=0):
@@ -243,3 +265,117 @@ def config_cycle():
 
 
 assert set(config_cycle()) == set(CONFIGURATIONS)
+
+
+# ---------------------------------------------------------------------------- pi0.5-shaped policy
+class Pi05Backbone(torch.nn.Module):
+    """pi0.5-shaped VLA policy: a Gemma-2B-like VLM over the prefix and a
+    Gemma-300M-like action expert run through ten flow-matching Euler steps.
+
+    * VLM: 18 layers, hidden 2048, 8 query heads / 1 KV head of 256, MLP 16384,
+      RMSNorm (1 + w), tanh-GELU gated MLP; the 256 image + 48 text prefix tokens
+      attend to one another bidirectionally, and every layer's rotated keys and
+      values are kept in a prefix cache.
+    * Action expert: 18 layers, width 1024, the same head layout (queries 8 x 256,
+      one KV head), MLP 4096.  Each layer of a denoise step attends to its VLM
+      layer's prefix cache plus the 50 action tokens' own keys and values.
+    * A denoise step embeds the noisy [50, 32] action chunk and the flow time,
+      runs the expert and projects back to a velocity; the sampler follows the
+      reference's frozen ten-step loop (actune/models/pi05.py:28-37): the time
+      tensor starts at float32(1) and adds float32(-1/10) in place after every
+      step, x_t = x_t + dt * v_t.
+
+    The image tokens are random bf16 embeddings of the stated count (no vision
+    encoder is specified); every projection of both stacks is a bank target."""
+
+    def __init__(self, vlm_layers=18, vlm_hidden=2048, vlm_mlp=16384, expert_layers=18, expert_hidden=1024,
+                 expert_mlp=4096, heads=8, kv_heads=1, head_dim=256, prefix_tokens=304, horizon=50, action_dim=32,
+                 steps=10, device="cuda", dtype=torch.bfloat16, seed=0):
+        super().__init__()
+        if vlm_layers != expert_layers:
+            raise ValueError("the action expert attends to the VLM layer of the same depth")
+        g = torch.Generator(device=device).manual_seed(seed)
+        kw = dict(device=device, dtype=dtype)
+        self.prefix_tokens, self.horizon, self.action_dim, self.steps = prefix_tokens, horizon, action_dim, steps
+        self.heads, self.kv_heads, self.head_dim = heads, kv_heads, head_dim
+        self.vlm = torch.nn.ModuleList([DecoderLayer(vlm_hidden, heads, kv_heads, head_dim, vlm_mlp, 1e-6, True,
+                                                     device, dtype) for _ in range(vlm_layers)])
+        self.expert = torch.nn.ModuleList([DecoderLayer(expert_hidden, heads, kv_heads, head_dim, expert_mlp, 1e-6,
+                                                        True, device, dtype) for _ in range(expert_layers)])
+        self.action_in = torch.nn.Linear(action_dim, expert_hidden, **kw)
+        self.time_in = torch.nn.Linear(expert_hidden, expert_hidden, **kw)
+        self.time_out = torch.nn.Linear(expert_hidden, expert_hidden, **kw)
+        self.action_out = torch.nn.Linear(expert_hidden, action_dim, **kw)
+        self.final_norm = torch.nn.Parameter(torch.zeros(expert_hidden, **kw))
+        with torch.no_grad():
+            for layer in list(self.vlm) + list(self.expert):
+                for lin in (layer.qkv_proj, layer.o_proj, layer.gate_up_proj, layer.down_proj):
+                    lin.weight.normal_(0.0, 0.02, generator=g)
+            for lin in (self.action_in, self.time_in, self.time_out, self.action_out):
+                lin.weight.normal_(0.0, 0.02, generator=g)
+                lin.bias.zero_()
+        cos, sin = rope_tables(prefix_tokens + horizon, head_dim, 10000.0, device)
+        self.register_buffer("rope_cos", cos)
+        self.register_buffer("rope_sin", sin)
+        half = expert_hidden // 2
+        freqs = torch.exp(-torch.arange(half, device=device, dtype=torch.float32) * (torch.log(torch.tensor(
+            10000.0, device=device)) / half))
+        self.register_buffer("time_freqs", freqs)
+        cache = torch.zeros(vlm_layers, 2, 1, kv_heads, prefix_tokens, head_dim, **kw)
+        self.register_buffer("prefix_cache", cache)
+
+    def prefix(self, embeds):
+        """VLM pass over the prefix tokens [304, 2048]: fills the prefix cache."""
+        x, residual = embeds, None
+        T = self.prefix_tokens
+        cos, sin = self.rope_cos[:T], self.rope_sin[:T]
+        for i, layer in enumerate(self.vlm):
+            x, residual = layer(x, residual, cos, sin, store=(self.prefix_cache[i, 0], self.prefix_cache[i, 1]),
+                                causal=False)
+        return self.prefix_cache
+
+    def velocity(self, x_t, time):
+        """v_t for the noisy chunk x_t [50, 32] (fp32) at flow time `time` (0-dim fp32)."""
+        T0, T = self.prefix_tokens, self.horizon
+        ang = time * self.time_freqs
+        temb = torch.cat([ang.sin(), ang.cos()]).to(self.action_in.weight.dtype)
+        tvec = self.time_out(F.silu(self.time_in(temb)))
+        x = self.action_in(x_t.to(self.action_in.weight.dtype)) + tvec
+        residual = None
+        cos, sin = self.rope_cos[T0:T0 + T], self.rope_sin[T0:T0 + T]
+        for i, layer in enumerate(self.expert):
+            x, residual = layer(x, residual, cos, sin, past=(self.prefix_cache[i, 0], self.prefix_cache[i, 1]),
+                                causal=False)
+        h, _ = rmsnorm(x, self.final_norm, 1e-6, residual, gemma=True)
+        return self.action_out(h).float()
+
+    def denoise_step(self, x_t, time, dt):
+        """One Euler step of the frozen sampler: (x_t + dt * v_t, time + dt)."""
+        v_t = self.velocity(x_t, time)
+        return x_t + dt * v_t, time + dt
+
+
+def make_pi05_policy(device="cuda", seed=0, **shape):
+    """Build the pi0.5-shaped backbone and install its W4A4-average bank (every
+    projection of both stacks W4A4, two binary switchable matrices W4A4 / W2A4)."""
+    model = Pi05Backbone(device=device, seed=seed, **shape)
+    tokens = {"vlm": model.prefix_tokens, "expert": model.horizon * model.steps}
+    bank, clips = build_bank(model, tokens, "w4a4", "w2a4", ("vlm.0.down_proj", "expert.0.down_proj"),
+                             stacks=("vlm", "expert"))
+    runtime = install_bank(model, bank, clips)
+    torch.cuda.synchronize()
+    return model, runtime
+
+
+def sample_pi05(model, prefix_call, step_call, embeds, noise):
+    """One action chunk: the prefix pass, then the frozen ten-step Euler loop with a
+    float32 time tensor that starts at 1 and adds float32(-1/steps) per step.
+    `prefix_call` / `step_call` are the model's prefix / denoise_step, or their
+    graph-replayed wrappers (one CUDA graph per step shape)."""
+    prefix_call(embeds)
+    dt = torch.tensor(-1.0 / model.steps, dtype=torch.float32, device=noise.device)
+    time = torch.tensor(1.0, dtype=torch.float32, device=noise.device)
+    x_t = noise
+    for _ in range(model.steps):
+        x_t, time = step_call(x_t, time, dt)
+    return x_t

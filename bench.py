@@ -45,6 +45,16 @@ WORKLOAD = ("config2: OpenVLA-OFT-shaped Llama-2-7B (32 layers, hidden 4096, MLP
             "q00/q01/q11/q10 cycled per call, CUDA graph per configuration")
 
 
+# pi0.5-shaped policy (bench.py --config 3).
+METRIC3 = "ms per action chunk (pi0.5-shape W4A4, prefix + 10 flow-matching steps)"
+P3 = dict(prefix=304, horizon=50, action_dim=32, steps=10, layers=18, vlm_hidden=2048, vlm_mlp=16384,
+          expert_hidden=1024, expert_mlp=4096, heads=8, kv_heads=1, head_dim=256)
+WORKLOAD3 = ("config3: pi0.5-shaped policy, Gemma-2B-like VLM (18 layers, hidden 2048, 8 heads / 1 KV head x 256, "
+             "MLP 16384) over 256 image + 48 text tokens, Gemma-300M-like action expert (width 1024, MLP 4096) "
+             "through 10 flow-matching Euler steps over a 50 x 32 Gaussian noise chunk, W4A4-average bank with two "
+             "switchable matrices, q00/q01/q11/q10 cycled per call, CUDA graph per step shape")
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -54,6 +64,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-sample-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, choices=[2, 3], default=2,
+                    help="2: OFT-shaped W4A8 backbone (the headline metric); 3: pi0.5-shaped W4A4 policy")
     return ap.parse_args()
 
 
@@ -69,52 +81,66 @@ def cpu_layer_weights(seed):
 
 
 class CpuLayer:
-    """One decoder layer evaluated with the reference's CPU dequantize-and-matmul
-    formula for every projection (reference tests/test_kernels.py:42-44:
-    F.linear(activation_reference(x, a), q.float() * scale[:, None])) and fp32
-    torch ops for norms, rotary embedding and attention.
+    """One pre-norm decoder layer evaluated with the reference's CPU
+    dequantize-and-matmul formula for every projection (reference
+    tests/test_kernels.py:42-44: F.linear(activation_reference(x, a),
+    q.float() * scale[:, None])) and fp32 torch ops for norms, rotary embedding,
+    attention and the gated activation.  The norm weights of the random-init
+    models are the identity, so the norms carry none.
 
     `weights` maps qkv / o / gu / down to bf16 [N, K] host tensors -- the same
-    values the GPU model is built from when the two are compared."""
+    values the GPU model is built from when the two are compared.  Defaults: the
+    OFT (Llama-2-7B) layer; the pi0.5 layers pass their Gemma shapes, `gemma`
+    (tanh-GELU gate) and the rotary position offset of their tokens."""
 
-    def __init__(self, weights, tokens=TOKENS):
+    def __init__(self, weights, tokens=TOKENS, heads=32, kv_heads=32, head_dim=128, gemma=False, w_bits=4,
+                 a_bits=8, rope_offset=0):
         import torch
         from oracle import oracle as O
-        self.tokens = tokens
+        self.tokens, self.heads, self.kv_heads, self.head_dim = tokens, heads, kv_heads, head_dim
+        self.gemma, self.a_bits = gemma, a_bits
         self.w = {}
         for name, wt in weights.items():
-            codes, scale = O.weight_codes(wt.float().numpy(), 4, 8)
+            codes, scale = O.weight_codes(wt.float().numpy(), w_bits, a_bits)
             self.w[name] = O.dequant_weight(torch.from_numpy(codes), torch.from_numpy(scale))  # hoisted
-        inv = 1.0 / (10000.0 ** (torch.arange(0, 128, 2, dtype=torch.float32) / 128))
-        ang = torch.arange(tokens, dtype=torch.float32)[:, None] * inv[None, :]
+        self.mlp = self.w["down"].shape[1]
+        half = head_dim // 2
+        inv = 1.0 / (10000.0 ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+        ang = torch.arange(rope_offset, rope_offset + tokens, dtype=torch.float32)[:, None] * inv[None, :half]
         self.cos, self.sin = ang.cos(), ang.sin()
 
-    def forward(self, x):
+    def forward(self, x, past=None, store=None, causal=True):
         import torch
         import torch.nn.functional as F
         from oracle import oracle as O
 
-        T = self.tokens
+        T, H, KV, D = self.tokens, self.heads, self.kv_heads, self.head_dim
 
         def norm(v):
-            return v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + 1e-5)
+            return v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + (1e-6 if self.gemma else 1e-5))
 
         def rope(t):
-            a, b = t[..., :64], t[..., 64:]
+            a, b = t[..., : D // 2], t[..., D // 2:]
             c, s = self.cos[:, None, :], self.sin[:, None, :]
             return torch.cat([a * c - b * s, b * c + a * s], -1)
 
-        h = norm(x)
-        qkv = O.dequant_linear(h, self.w["qkv"], None, 8)
-        q, k, v = qkv.split(HIDDEN, -1)
-        q = rope(q.view(T, 32, 128)).transpose(0, 1)
-        k = rope(k.view(T, 32, 128)).transpose(0, 1)
-        v = v.view(T, 32, 128).transpose(0, 1)
-        a = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(0, 1).reshape(T, HIDDEN)
-        x = x + O.dequant_linear(a, self.w["o"], None, 8)
-        gu = O.dequant_linear(norm(x), self.w["gu"], None, 8)
-        g, u = gu.split(MLP, -1)
-        return x + O.dequant_linear(F.silu(g) * u, self.w["down"], None, 8)
+        qkv = O.dequant_linear(norm(x), self.w["qkv"], None, self.a_bits)
+        q, k, v = qkv.split([H * D, KV * D, KV * D], -1)
+        q = rope(q.view(T, H, D)).transpose(0, 1)
+        k = rope(k.view(T, KV, D)).transpose(0, 1)
+        v = v.view(T, KV, D).transpose(0, 1)
+        if store is not None:
+            store.append((k, v))
+        if past is not None:
+            k, v = torch.cat([past[0], k], 1), torch.cat([past[1], v], 1)
+        if KV != H:
+            k, v = k.repeat_interleave(H // KV, 0), v.repeat_interleave(H // KV, 0)
+        a = F.scaled_dot_product_attention(q, k, v, is_causal=causal and past is None)
+        x = x + O.dequant_linear(a.transpose(0, 1).reshape(T, H * D), self.w["o"], None, self.a_bits)
+        gu = O.dequant_linear(norm(x), self.w["gu"], None, self.a_bits)
+        g, u = gu.split(self.mlp, -1)
+        act = F.gelu(g, approximate="tanh") if self.gemma else F.silu(g)
+        return x + O.dequant_linear(act * u, self.w["down"], None, self.a_bits)
 
 
 def cpu_chunk(layers, x0, n_layers=LAYERS):
@@ -178,6 +204,110 @@ def reference_arm(args):
                                        "cycled) of the reference's dequantize-and-matmul formula (oracle port), "
                                        f"{args.steps} timed steps after {args.warmup} warm-up"},
             "e2e": {"value": round(ms_step, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- config 3 on the CPU
+def pi05_cpu_weights(stack, seed):
+    """bf16 projection weights of one pi0.5 VLM or action-expert layer, N(0, 0.02)."""
+    import torch
+    hidden = P3["vlm_hidden"] if stack == "vlm" else P3["expert_hidden"]
+    mlp = P3["vlm_mlp"] if stack == "vlm" else P3["expert_mlp"]
+    hd, h, kv = P3["head_dim"], P3["heads"], P3["kv_heads"]
+    shapes = {"qkv": ((h + 2 * kv) * hd, hidden), "o": (hidden, h * hd), "gu": (2 * mlp, hidden),
+              "down": (hidden, mlp)}
+    g = torch.Generator().manual_seed(seed)
+    return {n: (torch.randn(r, c, generator=g) * 0.02).bfloat16() for n, (r, c) in shapes.items()}
+
+
+class Pi05Cpu:
+    """The pi0.5-shaped chunk with the reference's CPU formula in every projection:
+    the VLM over the prefix (keys and values kept per layer), then the frozen
+    ten-step Euler loop over the action expert (actune/models/pi05.py:28-37).
+    `vlm` / `expert` are lists of CpuLayer, cycled over the 18 layers."""
+
+    def __init__(self, vlm, expert, seed=0):
+        import torch
+        self.vlm, self.expert = vlm, expert
+        g = torch.Generator().manual_seed(seed)
+        w, a = P3["expert_hidden"], P3["action_dim"]
+        self.action_in = torch.randn(w, a, generator=g) * 0.02
+        self.time_in = torch.randn(w, w, generator=g) * 0.02
+        self.time_out = torch.randn(w, w, generator=g) * 0.02
+        self.action_out = torch.randn(a, w, generator=g) * 0.02
+        half = w // 2
+        self.freqs = torch.exp(-torch.arange(half, dtype=torch.float32) * (torch.log(torch.tensor(10000.0)) / half))
+
+    def chunk(self, embeds, noise, layers=P3["layers"]):
+        import torch
+        import torch.nn.functional as F
+        cache = []
+        x = embeds
+        for i in range(layers):
+            x = self.vlm[i % len(self.vlm)].forward(x, store=cache, causal=False)
+        dt = torch.tensor(-1.0 / P3["steps"], dtype=torch.float32)
+        time_ = torch.tensor(1.0, dtype=torch.float32)
+        x_t = noise
+        for _ in range(P3["steps"]):
+            ang = time_ * self.freqs
+            tvec = F.linear(F.silu(F.linear(torch.cat([ang.sin(), ang.cos()]), self.time_in)), self.time_out)
+            h = F.linear(x_t, self.action_in) + tvec
+            for i in range(layers):
+                h = self.expert[i % len(self.expert)].forward(h, past=cache[i], causal=False)
+            h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-6)
+            x_t = x_t + dt * F.linear(h, self.action_out)
+            time_ = time_ + dt
+        return x_t
+
+
+def pi05_cpu_model(weight_sets=2):
+    kw = dict(heads=P3["heads"], kv_heads=P3["kv_heads"], head_dim=P3["head_dim"], gemma=True, w_bits=4, a_bits=4)
+    vlm = [CpuLayer(pi05_cpu_weights("vlm", 200 + i), tokens=P3["prefix"], **kw) for i in range(weight_sets)]
+    expert = [CpuLayer(pi05_cpu_weights("expert", 300 + i), tokens=P3["horizon"], rope_offset=P3["prefix"], **kw)
+              for i in range(weight_sets)]
+    return Pi05Cpu(vlm, expert)
+
+
+def pi05_cpu_inputs():
+    import torch
+    g = torch.Generator().manual_seed(1)
+    embeds = torch.randn(P3["prefix"], P3["vlm_hidden"], generator=g).bfloat16().float()
+    noise = torch.randn(P3["horizon"], P3["action_dim"], generator=torch.Generator().manual_seed(0))
+    return embeds, noise
+
+
+def bench_config3(world):
+    return {"workload": WORKLOAD3, "prefix_tokens": P3["prefix"], "action_tokens": P3["horizon"],
+            "denoise_steps": P3["steps"], "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (1.15 GB packed weights streamed per chunk, L2 126 MB)"}
+
+
+def reference_arm3(args):
+    """Config 3 on the host cores: every step one whole chunk with the reference's
+    CPU formula (VLM prefix + ten expert passes, two weight sets cycled per stack)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.set_num_threads(os.cpu_count() or 1)
+    model = pi05_cpu_model()
+    embeds, noise = pi05_cpu_inputs()
+    for _ in range(args.warmup):
+        model.chunk(embeds, noise)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        model.chunk(embeds, noise)
+    ms = (time.perf_counter() - t0) / args.steps * 1e3
+    line = {"impl": "reference", "metric": METRIC3, "value": round(ms, 3), "unit": "ms", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "ms_per_chunk": round(ms, 3),
+            "chunks_per_step": 1, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic (seeded random prefix embeddings and noise, random-init weights)",
+            "config": bench_config3(world),
+            "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": "whole chunks (18 VLM layers over 304 tokens + 10 x 18 expert layers over 50 "
+                                       "tokens, two weight sets cycled per stack) of the reference's "
+                                       "dequantize-and-matmul formula (oracle port)"},
+            "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -396,8 +526,152 @@ def ours(args):
     return line
 
 
+def dominant_gemm3(torch, model):
+    """Device time of the pi0.5 VLM gate/up GEMM (W4A4, M=304, K=2048, N=32768), L2 flushed."""
+    from actune_b200 import ops
+    backend = model.vlm[0].gate_up_proj.backends["w4a4"]
+    k, n, m = P3["vlm_hidden"], 2 * P3["vlm_mlp"], P3["prefix"]
+    x = torch.randn(m, k, device="cuda").bfloat16()
+    pa, as_ = ops.quantize_group64(x, 4)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def launch():
+        ops.packed_linear(pa, as_, backend.packed_weight, backend.weight_scale, None, k, 4, 4, out=out)
+
+    for _ in range(3):
+        launch()
+    times = []
+    for _ in range(20):
+        flush.zero_()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        launch()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    return statistics.median(times) * 1e-3, 2 * m * n * k
+
+
+def ours3(args):
+    """Config 3 on the GPU: one step = one action chunk = the prefix graph plus ten
+    replays of the denoise-step graph (one CUDA graph per step shape and precision
+    configuration), precision cycled q00 -> q01 -> q11 -> q10 per chunk."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    from actune_b200.graph import GraphReplay
+    from actune_b200.harness import config_cycle, make_pi05_policy, sample_pi05
+    from actune_b200.precision import precision_profile
+
+    torch.manual_seed(4321 + rank)
+    model, runtime = make_pi05_policy(seed=rank)
+    prefix_replay = GraphReplay(model.prefix, runtime.modules, shared_a8=True, max_graphs=12)
+    step_replay = GraphReplay(model.denoise_step, runtime.modules, shared_a8=True, max_graphs=12)
+    prefix_replay.enabled = step_replay.enabled = True
+    cycle = config_cycle()
+    g = torch.Generator().manual_seed(7 + rank)
+    host_embeds = torch.randn(P3["prefix"], P3["vlm_hidden"], generator=g).bfloat16().pin_memory()
+    host_noise = torch.randn(P3["horizon"], P3["action_dim"], generator=g).pin_memory()
+    dev_embeds, dev_noise = host_embeds.to("cuda"), host_noise.to("cuda")
+    host_out = torch.empty(P3["horizon"], P3["action_dim"]).pin_memory()
+
+    def step(i, e2e=False):
+        with precision_profile(cycle[i % len(cycle)]), torch.inference_mode():
+            if e2e:
+                dev_embeds.copy_(host_embeds, non_blocking=True)
+                dev_noise.copy_(host_noise, non_blocking=True)
+            out = sample_pi05(model, prefix_replay, step_replay, dev_embeds, dev_noise)
+            if e2e:
+                host_out.copy_(out, non_blocking=True)
+        return out
+
+    for i in range(len(cycle)):
+        step(i)
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    def timed(e2e):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        for i in range(args.steps):
+            step(i, e2e)
+            if e2e:
+                torch.cuda.current_stream().synchronize()
+                _ = float(host_out[0, 0])
+        e.record()
+        e.synchronize()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = torch.tensor([s.elapsed_time(e) / args.steps], device="cuda")
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    with ClockSampler(local) as clocks:
+        ms_step = timed(False)
+    ms_step_e2e = timed(True)
+    clock_info = clocks.summary()
+    if rank == 0:
+        gemm_s, gemm_ops = dominant_gemm3(torch, model)
+        peak = int8_peak_tops(torch)
+        achieved = gemm_ops / gemm_s / 1e12
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            torch.set_num_threads(os.cpu_count() or 1)
+            cpu_model = pi05_cpu_model(weight_sets=1)
+            embeds, noise = pi05_cpu_inputs()
+            cpu_model.chunk(embeds, noise, layers=1)
+            t0 = time.perf_counter()
+            cpu_model.chunk(embeds, noise, layers=1)
+            secs = time.perf_counter() - t0
+            cpu = {"value": round(secs * P3["layers"] * 1e3, 1), "unit": "ms", "cores": torch.get_num_threads(),
+                   "kind": "port",
+                   "sample": "1 of 18 layers of each stack (the VLM prefix pass and ten expert passes) of the "
+                             "reference's CPU dequantize-and-matmul formula, scaled x18 to a chunk"}
+        launches = P3["layers"] * 11 + P3["steps"] * (P3["layers"] * 11 + 12)
+        line = {
+            "metric": METRIC3, "value": round(ms_step / world, 4), "unit": "ms", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "ms_per_chunk": round(ms_step / world, 4), "chunks_per_step": world,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded random prefix embeddings and Gaussian noise, random-init weights)",
+            "config": bench_config3(world),
+            "e2e": {"value": round(ms_step_e2e / world, 4), "unit": "ms",
+                    "h2d_bytes_per_step": host_embeds.numel() * 2 + host_noise.numel() * 4,
+                    "d2h_bytes_per_step": host_out.numel() * 4},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                         "unit": "TOP/s (int8)", "frac": round(achieved / peak, 4), "traffic": None,
+                         "kernel": "group64_gemm_kernel W4A4 M=304 K=2048 N=32768 (VLM gate/up)",
+                         "peak_source": "torch._int_mm int8 8192^3, measured in this run (of measured)",
+                         "gemm_us": round(gemm_s * 1e6, 2)},
+            "cpu_baseline": cpu, "clocks": clock_info, "gpu_launches": launches * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    prefix_replay.release()
+    step_replay.release()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
+    if args.config == 3:
+        (reference_arm3 if args.impl == "reference" else ours3)(args)
+        return
     if args.impl == "reference":
         reference_arm(args)
         return

@@ -227,3 +227,108 @@ def test_config2_two_full_width_layers_match_the_cpu_formula(ops):
     err = float((hidden - ref).abs().max())
     rms = float(ref.pow(2).mean().sqrt())
     assert rel <= 3e-2, (rel, err, rms)
+
+
+PI05 = {"vlm.qkv": (2048, 2560), "vlm.o": (2048, 2048), "vlm.gate_up": (2048, 32768), "vlm.down": (16384, 2048),
+        "expert.qkv": (1024, 2560), "expert.o": (2048, 1024), "expert.gate_up": (1024, 8192),
+        "expert.down": (4096, 1024)}
+
+
+@pytest.mark.parametrize("shape", list(PI05))
+def test_config3_projection_shapes(ops, shape):
+    """Config 3 (pi0.5-shaped, W4A4 bank with W2A4 switchable matrices): every
+    projection shape of both stacks at the prefix (M=304), a denoise step (M=50) and
+    the 16-environment serving batches (M=800 per step, 4864 per prefix), sampled
+    rows bit-exact (int32 dots and bf16 outputs) against the oracle."""
+    k, n = PI05[shape]
+    wt, x_all = seed0_operands(k, n, 4864)
+    failures = []
+    for (w, a) in ((4, 4), (2, 4)):
+        codes, ws = ops.weight_codes(wt.to(DEV), w, a)
+        pw = ops.pack_rows(codes, w)
+        pw_h, ws_h = pw.cpu().numpy(), ws.cpu().numpy()
+        for m in (50, 304, 800, 4864):
+            rows = sample_rows(m)
+            pa, as_ = ops.quantize_group64(x_all[:m].to(DEV), a)
+            y = ops.packed_linear(pa, as_, pw, ws, None, k, w, a, out_dtype=torch.bfloat16)
+            pa_h, as_h = pa.cpu().numpy()[rows], as_.cpu().numpy()[rows]
+            sub = torch.from_numpy(pa_h).to(DEV)
+            dots = ops.packed_linear_dots(sub, pw, k, w, a).cpu().numpy()
+            if not np.array_equal(dots, O.group_dots(pa_h, pw_h, k, w, a)):
+                failures.append(f"W{w}A{a} M={m}: int32 dots")
+            want = O.to_bf16_bits(O.packed_linear(pa_h, as_h, pw_h, ws_h, None, k, w, a, fma=True))
+            if not np.array_equal(bf16_bits(y)[rows], want):
+                failures.append(f"W{w}A{a} M={m}: bf16 outputs")
+    assert not failures, "; ".join(failures)
+
+
+def _small_pi05():
+    from actune_b200.harness import make_pi05_policy
+    return make_pi05_policy(seed=5, vlm_layers=2, vlm_hidden=256, vlm_mlp=512, expert_layers=2, expert_hidden=256,
+                            expert_mlp=256, heads=4, kv_heads=1, head_dim=64, prefix_tokens=40, horizon=8,
+                            action_dim=8)
+
+
+def test_config3_sampler_graph_replay_matches_eager_per_precision():
+    """The pi0.5 sampler through one CUDA graph per step shape (prefix, denoise
+    step) and precision configuration gives the eager chunk bit for bit, and the
+    layer counters advance as in eager execution."""
+    from actune_b200.graph import GraphReplay
+    from actune_b200.harness import sample_pi05
+    from actune_b200.precision import precision_profile
+    model, runtime = _small_pi05()
+    g = torch.Generator().manual_seed(9)
+    embeds = torch.randn(40, 256, generator=g).bfloat16().to(DEV)
+    noise = torch.randn(8, 8, generator=g).to(DEV)
+    eager = {}
+    runtime.before()
+    with torch.inference_mode():
+        for q in ("q00", "q01", "q11", "q10"):
+            with precision_profile(q):
+                eager[q] = sample_pi05(model, model.prefix, model.denoise_step, embeds, noise).clone()
+    eager_calls = {n: m.calls for n, m in runtime.modules.items()}
+    prefix = GraphReplay(model.prefix, runtime.modules, shared_a8=True)
+    step = GraphReplay(model.denoise_step, runtime.modules, shared_a8=True)
+    prefix.enabled = step.enabled = True
+    runtime.before()
+    for q in ("q00", "q01", "q11", "q10"):
+        with precision_profile(q), torch.inference_mode():
+            out = sample_pi05(model, prefix, step, embeds, noise).clone()
+        assert torch.equal(out, eager[q]), q
+    assert len(prefix.graphs) == 4 and len(step.graphs) == 4 and step.replays == 40
+    assert {n: m.calls for n, m in runtime.modules.items()} == eager_calls
+    assert eager["q00"].abs().sum() > 0
+    prefix.release()
+    step.release()
+
+
+def test_reuse_mlp_temporary_keeps_outputs():
+    """reuse_mlp_temporary (reference actune/kernels/grouped.py:18-36) patches every
+    Gemma MLP to reuse its gate buffer for the product: outputs are bit-identical
+    to the unpatched forward, and grad mode keeps the original forward."""
+    from transformers import GemmaConfig
+    from transformers.models.gemma.modeling_gemma import GemmaMLP
+    from actune_b200.kernels.grouped import reuse_mlp_temporary
+    from actune_b200.layers import install_bank
+    from actune_b200.precision import SharedBank, precision_profile
+    from actune_b200.layers import expected_version_bytes
+    cfg = GemmaConfig(hidden_size=256, intermediate_size=512, hidden_act="gelu_pytorch_tanh")
+    torch.manual_seed(2)
+    model = torch.nn.Sequential(GemmaMLP(cfg)).to(DEV, torch.bfloat16)
+    names = ["0.gate_proj", "0.up_proj", "0.down_proj"]
+    shapes = {n: [model.get_submodule(n).out_features, model.get_submodule(n).in_features] for n in names}
+    base = {n: "w4a8" for n in names}
+    configs = {"q11": dict(base), "q10": {**base, "0.down_proj": "w2a8"}, "q01": {**base, "0.up_proj": "w2a8"},
+               "q00": {**base, "0.up_proj": "w2a8", "0.down_proj": "w2a8"}}
+    vb = {n: {m: expected_version_bytes(*shapes[n], int(m[1]), int(m[3])) for m in {c[n] for c in configs.values()}}
+          for n in names}
+    bank = SharedBank(configs, shapes, {n: 8 * shapes[n][1] for n in names}, [[n] for n in names], vb, "w4a8",
+                      10 ** 8)
+    install_bank(model, bank, {n: {m: None for m in vb[n]} for n in names})
+    x = torch.randn(8, 256, device=DEV).bfloat16()
+    with torch.inference_mode(), precision_profile("q00"):
+        before = model(x).clone()
+    assert reuse_mlp_temporary(model) == 1 and reuse_mlp_temporary(model) == 0
+    with torch.inference_mode(), precision_profile("q00"):
+        after = model(x).clone()
+    assert torch.equal(before, after)
