@@ -35,7 +35,7 @@ def nvcc() -> str:
 
 
 def sources():
-    return sorted(CSRC.glob("*.cu"))
+    return sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cpp")))
 
 
 def _stale(target: Path, deps) -> bool:
