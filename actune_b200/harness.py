@@ -21,6 +21,8 @@ from __future__ import annotations
 
 import ctypes
 
+import numpy as np
+
 import torch
 import torch.nn.functional as F
 
@@ -138,22 +140,26 @@ class DecoderLayer(torch.nn.Module):
         self.gate_up_proj = torch.nn.Linear(hidden, 2 * mlp, bias=False, **kw)
         self.down_proj = torch.nn.Linear(mlp, hidden, bias=False, **kw)
 
-    def forward(self, x, residual, cos, sin, past=None, store=None, causal=True):
+    def forward(self, x, residual, cos, sin, past=None, store=None, causal=True, batch=1):
         """(x, residual) -> (mlp output, new residual stream), pre-norm.
 
-        `store`: (k, v) buffers [1, kv_heads, T, head_dim] that receive this call's
-        rotated keys and values (a prefix cache); `past`: such buffers from an
-        earlier call, prepended to this call's keys and values; `causal`: causal
-        attention within the call (bidirectional otherwise)."""
-        T = x.shape[0]
+        x holds `batch` independent sequences of T tokens as [batch * T, hidden]
+        rows (the projections see all rows at once; attention stays within each
+        sequence); cos / sin hold the rotary table of every row.  `store`: (k, v)
+        buffers [batch, kv_heads, T, head_dim] that receive this call's rotated keys
+        and values (a prefix cache); `past`: such buffers from an earlier call,
+        prepended to this call's keys and values; `causal`: causal attention within
+        the call (bidirectional otherwise)."""
+        rows = x.shape[0]
+        B, T = batch, rows // batch
         h, residual = rmsnorm(x, self.input_norm, self.eps, residual, self.gemma, input_bits(self.qkv_proj))
         qkv = self.qkv_proj(h)
         rope_(qkv, cos, sin, self.heads, self.kv_heads, self.head_dim)
         q, k, v = qkv.split([self.heads * self.head_dim, self.kv_heads * self.head_dim,
                              self.kv_heads * self.head_dim], dim=-1)
-        q = q.view(T, self.heads, self.head_dim).transpose(0, 1).unsqueeze(0)
-        k = k.view(T, self.kv_heads, self.head_dim).transpose(0, 1).unsqueeze(0)
-        v = v.view(T, self.kv_heads, self.head_dim).transpose(0, 1).unsqueeze(0)
+        q = q.view(B, T, self.heads, self.head_dim).transpose(1, 2)
+        k = k.view(B, T, self.kv_heads, self.head_dim).transpose(1, 2)
+        v = v.view(B, T, self.kv_heads, self.head_dim).transpose(1, 2)
         if store is not None:
             store[0].copy_(k)
             store[1].copy_(v)
@@ -162,7 +168,7 @@ class DecoderLayer(torch.nn.Module):
             v = torch.cat([past[1], v], dim=2)
         attn = F.scaled_dot_product_attention(q, k, v, is_causal=causal and past is None,
                                               enable_gqa=self.kv_heads != self.heads)
-        attn = attn.squeeze(0).transpose(0, 1).reshape(T, self.heads * self.head_dim)
+        attn = attn.transpose(1, 2).reshape(rows, self.heads * self.head_dim)
         x = self.o_proj(attn)
         h, residual = rmsnorm(x, self.post_norm, self.eps, residual, self.gemma, input_bits(self.gate_up_proj))
         x = self.down_proj(gated_act(self.gate_up_proj(h), gelu=self.gemma, quant_bits=input_bits(self.down_proj)))
@@ -290,13 +296,14 @@ class Pi05Backbone(torch.nn.Module):
 
     def __init__(self, vlm_layers=18, vlm_hidden=2048, vlm_mlp=16384, expert_layers=18, expert_hidden=1024,
                  expert_mlp=4096, heads=8, kv_heads=1, head_dim=256, prefix_tokens=304, horizon=50, action_dim=32,
-                 steps=10, device="cuda", dtype=torch.bfloat16, seed=0):
+                 steps=10, max_batch=1, state_dim=0, device="cuda", dtype=torch.bfloat16, seed=0):
         super().__init__()
         if vlm_layers != expert_layers:
             raise ValueError("the action expert attends to the VLM layer of the same depth")
         g = torch.Generator(device=device).manual_seed(seed)
         kw = dict(device=device, dtype=dtype)
         self.prefix_tokens, self.horizon, self.action_dim, self.steps = prefix_tokens, horizon, action_dim, steps
+        self.max_batch, self.state_dim = max_batch, state_dim
         self.heads, self.kv_heads, self.head_dim = heads, kv_heads, head_dim
         self.vlm = torch.nn.ModuleList([DecoderLayer(vlm_hidden, heads, kv_heads, head_dim, vlm_mlp, 1e-6, True,
                                                      device, dtype) for _ in range(vlm_layers)])
@@ -307,13 +314,17 @@ class Pi05Backbone(torch.nn.Module):
         self.time_out = torch.nn.Linear(expert_hidden, expert_hidden, **kw)
         self.action_out = torch.nn.Linear(expert_hidden, action_dim, **kw)
         self.final_norm = torch.nn.Parameter(torch.zeros(expert_hidden, **kw))
+        # Proprioceptive state, when the policy is given one: projected and added to
+        # every action token of its environment.
+        self.state_in = torch.nn.Linear(state_dim, expert_hidden, **kw) if state_dim else None
         with torch.no_grad():
             for layer in list(self.vlm) + list(self.expert):
                 for lin in (layer.qkv_proj, layer.o_proj, layer.gate_up_proj, layer.down_proj):
                     lin.weight.normal_(0.0, 0.02, generator=g)
-            for lin in (self.action_in, self.time_in, self.time_out, self.action_out):
-                lin.weight.normal_(0.0, 0.02, generator=g)
-                lin.bias.zero_()
+            for lin in (self.action_in, self.time_in, self.time_out, self.action_out, self.state_in):
+                if lin is not None:
+                    lin.weight.normal_(0.0, 0.02, generator=g)
+                    lin.bias.zero_()
         cos, sin = rope_tables(prefix_tokens + horizon, head_dim, 10000.0, device)
         self.register_buffer("rope_cos", cos)
         self.register_buffer("rope_sin", sin)
@@ -321,37 +332,56 @@ class Pi05Backbone(torch.nn.Module):
         freqs = torch.exp(-torch.arange(half, device=device, dtype=torch.float32) * (torch.log(torch.tensor(
             10000.0, device=device)) / half))
         self.register_buffer("time_freqs", freqs)
-        cache = torch.zeros(vlm_layers, 2, 1, kv_heads, prefix_tokens, head_dim, **kw)
+        cache = torch.zeros(vlm_layers, 2, max_batch, kv_heads, prefix_tokens, head_dim, **kw)
         self.register_buffer("prefix_cache", cache)
+        self._rope_rows = {}
+
+    def _rope(self, b, start, count):
+        """Rotary tables for b sequences of `count` positions from `start`, one row per token."""
+        key = (b, start, count)
+        if key not in self._rope_rows:
+            self._rope_rows[key] = (self.rope_cos[start:start + count].repeat(b, 1).contiguous(),
+                                    self.rope_sin[start:start + count].repeat(b, 1).contiguous())
+        return self._rope_rows[key]
 
     def prefix(self, embeds):
-        """VLM pass over the prefix tokens [304, 2048]: fills the prefix cache."""
-        x, residual = embeds, None
+        """VLM pass over the prefix tokens ([304, 2048], or [b, 304, 2048] for b
+        environments): fills the first b entries of the prefix cache."""
+        b = 1 if embeds.dim() == 2 else embeds.shape[0]
+        if b > self.max_batch:
+            raise ValueError("batch larger than the prefix cache")
         T = self.prefix_tokens
-        cos, sin = self.rope_cos[:T], self.rope_sin[:T]
+        x, residual = embeds.reshape(b * T, -1), None
+        cos, sin = self._rope(b, 0, T)
         for i, layer in enumerate(self.vlm):
-            x, residual = layer(x, residual, cos, sin, store=(self.prefix_cache[i, 0], self.prefix_cache[i, 1]),
-                                causal=False)
+            x, residual = layer(x, residual, cos, sin, store=(self.prefix_cache[i, 0, :b], self.prefix_cache[i, 1, :b]),
+                                causal=False, batch=b)
         return self.prefix_cache
 
-    def velocity(self, x_t, time):
-        """v_t for the noisy chunk x_t [50, 32] (fp32) at flow time `time` (0-dim fp32)."""
+    def velocity(self, x_t, time, state=None):
+        """v_t for the noisy chunk x_t ([50, 32], or [b, 50, 32]; fp32) at flow time
+        `time` (0-dim fp32), attending to the first b prefix caches."""
+        b = 1 if x_t.dim() == 2 else x_t.shape[0]
         T0, T = self.prefix_tokens, self.horizon
+        dtype = self.action_in.weight.dtype
         ang = time * self.time_freqs
-        temb = torch.cat([ang.sin(), ang.cos()]).to(self.action_in.weight.dtype)
+        temb = torch.cat([ang.sin(), ang.cos()]).to(dtype)
         tvec = self.time_out(F.silu(self.time_in(temb)))
-        x = self.action_in(x_t.to(self.action_in.weight.dtype)) + tvec
+        x = self.action_in(x_t.reshape(b * T, -1).to(dtype)) + tvec
+        if state is not None and self.state_in is not None:
+            x = (x.view(b, T, -1) + self.state_in(state.to(dtype))[:, None, :]).reshape(b * T, -1)
         residual = None
-        cos, sin = self.rope_cos[T0:T0 + T], self.rope_sin[T0:T0 + T]
+        cos, sin = self._rope(b, T0, T)
         for i, layer in enumerate(self.expert):
-            x, residual = layer(x, residual, cos, sin, past=(self.prefix_cache[i, 0], self.prefix_cache[i, 1]),
-                                causal=False)
+            x, residual = layer(x, residual, cos, sin,
+                                past=(self.prefix_cache[i, 0, :b], self.prefix_cache[i, 1, :b]), causal=False,
+                                batch=b)
         h, _ = rmsnorm(x, self.final_norm, 1e-6, residual, gemma=True)
-        return self.action_out(h).float()
+        return self.action_out(h).float().view(x_t.shape)
 
-    def denoise_step(self, x_t, time, dt):
+    def denoise_step(self, x_t, time, dt, state=None):
         """One Euler step of the frozen sampler: (x_t + dt * v_t, time + dt)."""
-        v_t = self.velocity(x_t, time)
+        v_t = self.velocity(x_t, time, state)
         return x_t + dt * v_t, time + dt
 
 
@@ -367,7 +397,7 @@ def make_pi05_policy(device="cuda", seed=0, **shape):
     return model, runtime
 
 
-def sample_pi05(model, prefix_call, step_call, embeds, noise):
+def sample_pi05(model, prefix_call, step_call, embeds, noise, state=None):
     """One action chunk: the prefix pass, then the frozen ten-step Euler loop with a
     float32 time tensor that starts at 1 and adds float32(-1/steps) per step.
     `prefix_call` / `step_call` are the model's prefix / denoise_step, or their
@@ -377,5 +407,64 @@ def sample_pi05(model, prefix_call, step_call, embeds, noise):
     time = torch.tensor(1.0, dtype=torch.float32, device=noise.device)
     x_t = noise
     for _ in range(model.steps):
-        x_t, time = step_call(x_t, time, dt)
+        x_t, time = step_call(x_t, time, dt) if state is None else step_call(x_t, time, dt, state)
     return x_t
+
+
+# ---------------------------------------------------------------------------- pi0.5 serving replica
+class Pi05Serving:
+    """One serving replica of the pi0.5-shaped policy: `envs` environments, each
+    request a 224 x 224 x 3 uint8 image and a 14-dim proprioceptive state.
+
+    The image goes through a patch stem (14 x 14 patches -> 256 tokens, one bf16
+    linear 588 -> 2048; no vision encoder is specified) and is followed by 48
+    prompt-token embeddings; the state is projected onto the action tokens.  A
+    group of environments sharing a configuration is padded to a batch bucket and
+    runs one prefix graph and ten denoise-step graphs (one CUDA graph per bucket,
+    step shape and configuration)."""
+
+    PATCH, IMAGE, TEXT = 14, 224, 48
+
+    def __init__(self, envs=16, buckets=(4, 8, 16), seed=0, device="cuda", **shape):
+        from .graph import GraphReplay
+        self.envs, self.buckets, self.device = envs, tuple(buckets), device
+        self.model, self.runtime = make_pi05_policy(device=device, seed=seed, max_batch=max(buckets), state_dim=14,
+                                                    **shape)
+        m = self.model
+        hidden = m.vlm[0].hidden
+        g = torch.Generator(device=device).manual_seed(seed + 1)
+        self.stem = torch.nn.Linear(self.PATCH * self.PATCH * 3, hidden, device=device, dtype=torch.bfloat16)
+        with torch.no_grad():
+            self.stem.weight.normal_(0.0, 0.02, generator=g)
+            self.stem.bias.zero_()
+        self.text = (torch.randn(self.TEXT, hidden, device=device, generator=g) * 0.5).bfloat16()
+        self.patches = (self.IMAGE // self.PATCH) ** 2
+        if self.patches + self.TEXT != m.prefix_tokens:
+            raise ValueError("prefix tokens must be 256 image patches + 48 prompt tokens")
+        self.prefix = GraphReplay(self._prefix, self.runtime.modules, shared_a8=True, max_graphs=4 * len(buckets))
+        self.step = GraphReplay(m.denoise_step, self.runtime.modules, shared_a8=True, max_graphs=4 * len(buckets))
+        self.prefix.enabled = self.step.enabled = True
+        gn = torch.Generator(device=device).manual_seed(seed + 2)
+        self.noise = torch.randn(max(buckets), m.horizon, m.action_dim, device=device, generator=gn)
+
+    def _prefix(self, images):
+        """uint8 images [b, 224, 224, 3] -> the VLM prefix pass over [b, 304, hidden]."""
+        b, P = images.shape[0], self.PATCH
+        x = images.view(b, self.IMAGE // P, P, self.IMAGE // P, P, 3).permute(0, 1, 3, 2, 4, 5)
+        x = x.reshape(b, self.patches, P * P * 3).to(torch.bfloat16) * (2.0 / 255.0) - 1.0
+        tokens = torch.cat([self.stem(x), self.text.expand(b, -1, -1)], dim=1)
+        return self.model.prefix(tokens)
+
+    def chunk(self, config, images, states, rows, size):
+        """Actions [len(rows), 50, 32] (device) for the environments `rows` of the
+        device batches images [envs, ...] / states [envs, 14], padded to `size`."""
+        from .precision import precision_profile
+        idx = torch.as_tensor(np.pad(rows, (0, size - len(rows)), mode="edge"), device=self.device)
+        with precision_profile(config), torch.inference_mode():
+            out = sample_pi05(self.model, self.prefix, self.step, images.index_select(0, idx),
+                              self.noise[:size], states.index_select(0, idx))
+        return out[: len(rows)]
+
+    def release(self):
+        self.prefix.release()
+        self.step.release()

@@ -55,6 +55,16 @@ WORKLOAD3 = ("config3: pi0.5-shaped policy, Gemma-2B-like VLM (18 layers, hidden
              "switchable matrices, q00/q01/q11/q10 cycled per call, CUDA graph per step shape")
 
 
+# serving (bench.py --config 4).
+METRIC4 = "aggregate action chunks/s (pi0.5-shape serving, 16 environments per GPU, per-request precision routing)"
+ENVS4 = 16
+WORKLOAD4 = ("config4: one replica of the config-3 pi0.5-shaped W4A4 policy per GPU serving 16 independent "
+             "environments (224x224x3 uint8 image + 14-dim N(0,1) state per request); each request's "
+             "configuration chosen by a random depth<=5, 3-leaf selector tree over the 13 action-history "
+             "features + state (C++ router) with a two-request minimum dwell; environments grouped by "
+             "configuration into batches of 4/8/16, one CUDA graph per batch, step shape and configuration")
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -64,8 +74,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-sample-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=[2, 3], default=2,
-                    help="2: OFT-shaped W4A8 backbone (the headline metric); 3: pi0.5-shaped W4A4 policy")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4], default=2,
+                    help="2: OFT-shaped W4A8 backbone (the headline metric); 3: pi0.5-shaped W4A4 policy; "
+                         "4: serving 16 environments per GPU with per-request routing")
     return ap.parse_args()
 
 
@@ -667,10 +678,188 @@ def ours3(args):
         dist.destroy_process_group()
 
 
+def bench_config4(world):
+    return {"workload": WORKLOAD4, "envs_per_gpu": ENVS4, "prefix_tokens": P3["prefix"],
+            "denoise_steps": P3["steps"], "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (1.15 GB packed weights streamed per batch, L2 126 MB)"}
+
+
+def ours4(args):
+    """Config 4: one step = one request round for all 16 environments of the
+    replica (routing, dwell, grouping, batched chunks, actions back to the host)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    from actune_b200.harness import Pi05Serving
+    from actune_b200.router import PrecisionTree, random_selector_tree
+    from actune_b200.serving import EnvRouter, groups_by_configuration
+
+    torch.manual_seed(99 + rank)
+    serving = Pi05Serving(envs=ENVS4, seed=rank)
+    rng = np.random.default_rng(1000 + rank)
+    pool = 4  # distinct image / state sets cycled over the requests
+    host_images = torch.from_numpy(rng.integers(0, 256, (pool, ENVS4, 224, 224, 3), dtype=np.uint8)).pin_memory()
+    host_states = torch.from_numpy(rng.standard_normal((pool, ENVS4, 14)).astype(np.float32)).pin_memory()
+    dev_images = host_images.to("cuda")
+    dev_states = host_states.to("cuda")
+    host_actions = torch.empty(ENVS4, P3["horizon"], P3["action_dim"]).pin_memory()
+
+    def round_(i, router, e2e):
+        k = i % pool
+        if e2e:
+            img = dev_images[0]
+            img.copy_(host_images[k], non_blocking=True)
+            st = dev_states[0]
+            st.copy_(host_states[k], non_blocking=True)
+        else:
+            img, st = dev_images[k], dev_states[k]
+        configs = router.assign(host_states[k].numpy())
+        for c, envs, size in groups_by_configuration(configs, serving.buckets):
+            out = serving.chunk(("q00", "q01", "q11", "q10")[c], img, st, envs, size)
+            host_actions[torch.as_tensor(envs)] = out.cpu()
+        router.observe(host_actions.numpy())
+
+    # Selector tree: three leaves over the action features and the state, with
+    # thresholds at medians of the values a first request produces.
+    probe = EnvRouter(PrecisionTree({"profile_index": 2}, 14), ENVS4)
+    round_(0, probe, False)
+    x = np.concatenate([probe.features, host_states[0].numpy()], 1)
+    med = {f: (lambda v: (lambda r: v))(float(np.median(x[:, f]))) for f in range(27)}
+    tree = PrecisionTree(random_selector_tree(np.random.default_rng(7), 14, leaves=3, thresholds=med), 14)
+    router = EnvRouter(tree, ENVS4)
+    # Capture every bucket x configuration graph once, then warm up.
+    for c in ("q00", "q01", "q11", "q10"):
+        for b in serving.buckets:
+            serving.chunk(c, dev_images[0], dev_states[0], np.arange(b), b)
+    for i in range(args.warmup):
+        round_(i, router, False)
+    torch.cuda.synchronize()
+
+    def timed(e2e):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        for i in range(args.steps):
+            round_(i, router, e2e)
+        e.record()
+        e.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = torch.tensor([s.elapsed_time(e) / args.steps], device="cuda")
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    with ClockSampler(local) as clocks:
+        ms_round = timed(False)
+    ms_round_e2e = timed(True)
+    clock_info = clocks.summary()
+    if rank == 0:
+        from actune_b200 import ops
+        backend = serving.model.vlm[0].gate_up_proj.backends["w4a4"]
+        m, k, n = ENVS4 * P3["prefix"], P3["vlm_hidden"], 2 * P3["vlm_mlp"]
+        xq = torch.randn(m, k, device="cuda").bfloat16()
+        pa, as_ = ops.quantize_group64(xq, 4)
+        out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        times = []
+        for r in range(13):
+            flush.zero_()
+            s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+            s.record()
+            ops.packed_linear(pa, as_, backend.packed_weight, backend.weight_scale, None, k, 4, 4, out=out)
+            e.record()
+            e.synchronize()
+            if r >= 3:
+                times.append(s.elapsed_time(e) * 1e-3)
+        gemm_s = statistics.median(times)
+        peak = int8_peak_tops(torch)
+        achieved = 2 * m * n * k / gemm_s / 1e12
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            torch.set_num_threads(os.cpu_count() or 1)
+            cpu_model = pi05_cpu_model(weight_sets=1)
+            embeds, noise = pi05_cpu_inputs()
+            cpu_model.chunk(embeds, noise, layers=1)
+            t0 = time.perf_counter()
+            cpu_model.chunk(embeds, noise, layers=1)
+            secs = (time.perf_counter() - t0) * P3["layers"]
+            cpu = {"value": round(1.0 / secs, 4), "unit": "chunks/s", "cores": torch.get_num_threads(),
+                   "kind": "port",
+                   "sample": "one environment's chunk, 1 of 18 layers of each stack of the reference's CPU "
+                             "dequantize-and-matmul formula timed and scaled x18 (environments served one "
+                             "after another on the host cores)"}
+        chunks_per_s = world * ENVS4 / (ms_round * 1e-3)
+        line = {
+            "metric": METRIC4, "value": round(chunks_per_s, 2), "unit": "chunks/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_round, 3),
+            "chunks_per_step": world * ENVS4, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic (uniform uint8 images, N(0,1) states, random-init weights)",
+            "config": bench_config4(world),
+            "e2e": {"value": round(world * ENVS4 / (ms_round_e2e * 1e-3), 2), "unit": "chunks/s",
+                    "h2d_bytes_per_step": ENVS4 * (224 * 224 * 3 + 14 * 4),
+                    "d2h_bytes_per_step": ENVS4 * P3["horizon"] * P3["action_dim"] * 4},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                         "unit": "TOP/s (int8)", "frac": round(achieved / peak, 4), "traffic": None,
+                         "kernel": f"group64_gemm_kernel W4A4 M={m} K={k} N={n} (VLM gate/up, 16 environments)",
+                         "peak_source": "torch._int_mm int8 8192^3, measured in this run (of measured)",
+                         "gemm_us": round(gemm_s * 1e6, 2)},
+            "routing": {"switches": int(router.switches), "rounds": args.warmup + 2 * args.steps},
+            "cpu_baseline": cpu, "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    serving.release()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def reference_arm4(args):
+    """Config 4 on the host cores: the reference's CPU formula serves the
+    environments one chunk at a time; each step is one environment's chunk."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.set_num_threads(os.cpu_count() or 1)
+    model = pi05_cpu_model()
+    embeds, noise = pi05_cpu_inputs()
+    for _ in range(args.warmup):
+        model.chunk(embeds, noise)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        model.chunk(embeds, noise)
+    secs = (time.perf_counter() - t0) / args.steps
+    rate = 1.0 / secs
+    line = {"impl": "reference", "metric": METRIC4, "value": round(rate, 4), "unit": "chunks/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs * 1e3, 3), "chunks_per_step": 1,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded random prefix embeddings and noise, random-init weights)",
+            "config": bench_config4(world),
+            "cpu_baseline": {"value": round(rate, 4), "unit": "chunks/s", "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": "one environment's whole chunk per step (reference's "
+                                                       "dequantize-and-matmul formula, oracle port)"},
+            "e2e": {"value": round(rate, 4), "unit": "chunks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.config == 3:
         (reference_arm3 if args.impl == "reference" else ours3)(args)
+        return
+    if args.config == 4:
+        (reference_arm4 if args.impl == "reference" else ours4)(args)
         return
     if args.impl == "reference":
         reference_arm(args)
