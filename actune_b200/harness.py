@@ -140,33 +140,35 @@ class DecoderLayer(torch.nn.Module):
         self.gate_up_proj = torch.nn.Linear(hidden, 2 * mlp, bias=False, **kw)
         self.down_proj = torch.nn.Linear(mlp, hidden, bias=False, **kw)
 
-    def forward(self, x, residual, cos, sin, past=None, store=None, causal=True, batch=1):
+    def forward(self, x, residual, cos, sin, causal=True, batch=1, cache=None, offset=0):
         """(x, residual) -> (mlp output, new residual stream), pre-norm.
 
         x holds `batch` independent sequences of T tokens as [batch * T, hidden]
         rows (the projections see all rows at once; attention stays within each
-        sequence); cos / sin hold the rotary table of every row.  `store`: (k, v)
-        buffers [batch, kv_heads, T, head_dim] that receive this call's rotated keys
-        and values (a prefix cache); `past`: such buffers from an earlier call,
-        prepended to this call's keys and values; `causal`: causal attention within
-        the call (bidirectional otherwise)."""
+        sequence); cos / sin hold the rotary table of every row; `causal`: causal
+        attention within the call (bidirectional otherwise).
+
+        `cache`: a key/value buffer [batch, T_cache, 2, head_dim] (one KV head) for
+        this layer.  The call's rotated keys and values are written at positions
+        [offset, offset + T) with one copy, and attention runs over positions
+        [0, offset + T) -- the prefix cached by earlier calls plus this call."""
         rows = x.shape[0]
         B, T = batch, rows // batch
         h, residual = rmsnorm(x, self.input_norm, self.eps, residual, self.gemma, input_bits(self.qkv_proj))
         qkv = self.qkv_proj(h)
         rope_(qkv, cos, sin, self.heads, self.kv_heads, self.head_dim)
-        q, k, v = qkv.split([self.heads * self.head_dim, self.kv_heads * self.head_dim,
-                             self.kv_heads * self.head_dim], dim=-1)
-        q = q.view(B, T, self.heads, self.head_dim).transpose(1, 2)
-        k = k.view(B, T, self.kv_heads, self.head_dim).transpose(1, 2)
-        v = v.view(B, T, self.kv_heads, self.head_dim).transpose(1, 2)
-        if store is not None:
-            store[0].copy_(k)
-            store[1].copy_(v)
-        if past is not None:
-            k = torch.cat([past[0], k], dim=2)
-            v = torch.cat([past[1], v], dim=2)
-        attn = F.scaled_dot_product_attention(q, k, v, is_causal=causal and past is None,
+        qd, kvd = self.heads * self.head_dim, self.kv_heads * self.head_dim
+        q = qkv[:, :qd].view(B, T, self.heads, self.head_dim).transpose(1, 2)
+        if cache is None:
+            k = qkv[:, qd:qd + kvd].view(B, T, self.kv_heads, self.head_dim).transpose(1, 2)
+            v = qkv[:, qd + kvd:].view(B, T, self.kv_heads, self.head_dim).transpose(1, 2)
+        else:
+            if self.kv_heads != 1:
+                raise ValueError("the key/value cache holds one KV head")
+            cache[:, offset:offset + T].copy_(qkv[:, qd:].view(B, T, 2, self.head_dim))
+            k = cache[:, :offset + T, 0].unsqueeze(1)
+            v = cache[:, :offset + T, 1].unsqueeze(1)
+        attn = F.scaled_dot_product_attention(q, k, v, is_causal=causal and offset == 0,
                                               enable_gqa=self.kv_heads != self.heads)
         attn = attn.transpose(1, 2).reshape(rows, self.heads * self.head_dim)
         x = self.o_proj(attn)
@@ -332,7 +334,11 @@ class Pi05Backbone(torch.nn.Module):
         freqs = torch.exp(-torch.arange(half, device=device, dtype=torch.float32) * (torch.log(torch.tensor(
             10000.0, device=device)) / half))
         self.register_buffer("time_freqs", freqs)
-        cache = torch.zeros(vlm_layers, 2, max_batch, kv_heads, prefix_tokens, head_dim, **kw)
+        if kv_heads != 1:
+            raise ValueError("the pi0.5 layout has one KV head")
+        # Per VLM layer: keys and values of the prefix, then room for the action
+        # tokens of a denoise step (written by the expert layer of the same depth).
+        cache = torch.zeros(vlm_layers, max_batch, prefix_tokens + horizon, 2, head_dim, **kw)
         self.register_buffer("prefix_cache", cache)
         self._rope_rows = {}
 
@@ -354,8 +360,8 @@ class Pi05Backbone(torch.nn.Module):
         x, residual = embeds.reshape(b * T, -1), None
         cos, sin = self._rope(b, 0, T)
         for i, layer in enumerate(self.vlm):
-            x, residual = layer(x, residual, cos, sin, store=(self.prefix_cache[i, 0, :b], self.prefix_cache[i, 1, :b]),
-                                causal=False, batch=b)
+            x, residual = layer(x, residual, cos, sin, causal=False, batch=b, cache=self.prefix_cache[i, :b, :T],
+                                offset=0)
         return self.prefix_cache
 
     def velocity(self, x_t, time, state=None):
@@ -373,9 +379,8 @@ class Pi05Backbone(torch.nn.Module):
         residual = None
         cos, sin = self._rope(b, T0, T)
         for i, layer in enumerate(self.expert):
-            x, residual = layer(x, residual, cos, sin,
-                                past=(self.prefix_cache[i, 0, :b], self.prefix_cache[i, 1, :b]), causal=False,
-                                batch=b)
+            x, residual = layer(x, residual, cos, sin, causal=False, batch=b, cache=self.prefix_cache[i, :b],
+                                offset=T0)
         h, _ = rmsnorm(x, self.final_norm, 1e-6, residual, gemma=True)
         return self.action_out(h).float().view(x_t.shape)
 
