@@ -74,9 +74,10 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-sample-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4], default=2,
-                    help="2: OFT-shaped W4A8 backbone (the headline metric); 3: pi0.5-shaped W4A4 policy; "
-                         "4: serving 16 environments per GPU with per-request routing")
+    ap.add_argument("--config", type=int, choices=[0, 1, 2, 3, 4], default=2,
+                    help="2: OFT-shaped W4A8 backbone (the headline metric); 0: one W4A8 linear; 1: the 180-case "
+                         "precision sweep; 3: pi0.5-shaped W4A4 policy; 4: serving 16 environments per GPU")
+    ap.add_argument("--markdown", default=None, help="config 1: also write the per-case table here")
     return ap.parse_args()
 
 
@@ -853,8 +854,145 @@ def reference_arm4(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------- configs 0 and 1
+_DEQUANT = {}
+
+
+def cpu_formula_ms(m, k, n, w, a, threads, repeats=3):
+    """Median ms of the reference's CPU dequantize-and-matmul formula for one linear
+    (the weight dequantization hoisted and cached per shape and pair), on `threads`
+    host threads."""
+    import torch
+    from oracle import oracle as O
+    torch.set_num_threads(threads)
+    key = (k, n, w, a)
+    if key not in _DEQUANT:
+        g = torch.Generator().manual_seed(k + n)
+        wt = (torch.randn(n, k, generator=g) * 0.02).bfloat16().float()
+        codes, scale = O.weight_codes(wt.numpy(), w, a)
+        _DEQUANT.clear()  # one shape at a time keeps host memory bounded
+        _DEQUANT[key] = O.dequant_weight(torch.from_numpy(codes), torch.from_numpy(scale))
+    wd = _DEQUANT[key]
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(m)).bfloat16().float()
+    O.dequant_linear(x, wd, None, a)
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        O.dequant_linear(x, wd, None, a)
+        times.append((time.perf_counter() - t0) * 1e3)
+    return statistics.median(times)
+
+
+def config0(args):
+    """one W4A8 linear, M=256, K=N=4096 (seed-0 recipe shapes):
+    device time of the packed linear (L2 flushed, graph-replayed), the same call
+    end to end from host buffers, and the CPU formula at all threads and at 1."""
+    import torch
+    from actune_b200 import ops
+    from actune_b200.sweep import _graph_us, _int8_peak_tops
+    m, k, n, w, a = 256, 4096, 4096, 4, 8
+    torch.manual_seed(0)
+    wt = (torch.randn(n, k) * 0.02).bfloat16().cuda()
+    x = torch.randn(m, k)
+    x[:, torch.randperm(k, generator=torch.Generator().manual_seed(0))[:41]] *= 20.0
+    host_x = x.bfloat16().pin_memory()
+    codes, ws = ops.weight_codes(wt, w, a)
+    pw = ops.pack_rows(codes, w)
+    dev_x = host_x.cuda()
+    pa, as_ = ops.quantize_group64(dev_x, a)
+    y = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    us = _graph_us(lambda: ops.packed_linear(pa, as_, pw, ws, None, k, w, a, out=y), flush, 10)
+    host_y = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+    workspace = torch.empty(ops.workspace_size(m, k, a), device="cuda", dtype=torch.uint8)
+
+    def e2e_call():
+        dev_x.copy_(host_x, non_blocking=True)
+        ops.grouped_linear(dev_x, pw, ws, None, w, a, workspace=workspace, out=y)
+        host_y.copy_(y, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(args.warmup):
+        e2e_call()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_call()
+    e2e_us = (time.perf_counter() - t0) / args.steps * 1e6
+    peak = _int8_peak_tops(torch.device("cuda"))
+    tops = 2 * m * n * k / us / 1e6
+    cores = os.cpu_count() or 1
+    cpu_all = cpu_formula_ms(m, k, n, w, a, cores)
+    cpu_one = cpu_formula_ms(m, k, n, w, a, 1)
+    print(json.dumps({
+        "metric": "us per W4A8 linear (config 0: M=256, K=N=4096)", "value": round(us, 2), "unit": "us",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seed-0 recipe shapes, 41 outlier channels x20)",
+        "config": {"workload": "config0: one group-64 W4A8 linear, M=256, K=N=4096, no bias",
+                   "l2": "flushed between calls (64 Mi floats written)"},
+        "e2e": {"value": round(e2e_us, 2), "unit": "us", "h2d_bytes_per_step": m * k * 2,
+                "d2h_bytes_per_step": m * n * 2, "path": "actune_grouped_linear (quantize + GEMM)"},
+        "roofline": {"bound": "tensor", "achieved": round(tops, 1), "peak": round(peak, 1), "unit": "TOP/s (int8)",
+                     "frac": round(tops / peak, 4), "traffic": None},
+        "cpu_baseline": {"value": round(cpu_all * 1e3, 1), "unit": "us", "cores": cores, "kind": "port",
+                         "sample": "the whole linear (reference's dequantize-and-matmul formula, weights dequantized "
+                                   "outside the timed region)", "one_thread_us": round(cpu_one * 1e3, 1)}}),
+        flush=True)
+
+
+def config1(args):
+    """all nine pairs x four Llama projection shapes x M in
+    {1, 8, 64, 256, 512}: device time per case (actune_b200.sweep: L2 flushed,
+    graph-replayed) next to the CPU formula for the same case on all host threads
+    (and on one thread for the single-token and 64-token cases)."""
+    import torch
+    from actune_b200 import sweep
+    pairs = [(w, a) for w in (2, 4, 8) for a in (2, 4, 8)]
+    ms = (1, 8, 64, 256, 512)
+    result = sweep.run(pairs, ms, list(sweep.SHAPES), reps=10)
+    cores = os.cpu_count() or 1
+    cpu = {}
+    for name, (k, n) in sweep.SHAPES.items():
+        for (w, a) in pairs:
+            for m in ms:
+                cpu[(w, a, name, m)] = cpu_formula_ms(m, k, n, w, a, cores, repeats=1)
+                if (w, a) == (4, 8):
+                    cpu[("1t", name, m)] = cpu_formula_ms(m, k, n, 4, 8, 1, repeats=1) if m <= 64 else None
+    total_gpu = sum(r["us"] for r in result["rows"])
+    total_cpu = sum(cpu[(r["W"], r["A"], r["shape"], r["M"])] * 1e3 for r in result["rows"])
+    for r in result["rows"]:
+        r["cpu_us"] = round(cpu[(r["W"], r["A"], r["shape"], r["M"])] * 1e3, 1)
+        one = cpu[("1t", r["shape"], r["M"])]
+        r["cpu_1t_us_w4a8"] = None if one is None else round(one * 1e3, 1)
+    if args.markdown:
+        lines = [f"GPU: one B200, HBM peak {result['hbm_gbs']:.0f} GB/s (MEASURED_PEAKS.json), INT8 peak "
+                 f"{result['int8_tops']:.0f} TOP/s (torch._int_mm 8192^3, same run).  CPU: the reference's "
+                 f"dequantize-and-matmul formula on {cores} host threads (1-thread column: the W4A8 case).", "",
+                 "| pair | shape | M | GPU us | of HBM | of INT8 | CPU us | CPU 1-thread us |",
+                 "|---|---|---|---|---|---|---|---|"]
+        for r in result["rows"]:
+            lines.append(f"| W{r['W']}A{r['A']} | {r['shape']} | {r['M']} | {r['us']} | {r['hbm_frac']} | "
+                         f"{r['int8_frac']} | {r['cpu_us']} | {r['cpu_1t_us_w4a8'] or ''} |")
+        Path(args.markdown).write_text("\n".join(lines) + "\n")
+    print(json.dumps({
+        "metric": "us for the 180-case precision sweep (config 1, sum over cases)", "value": round(total_gpu, 1),
+        "unit": "us", "n_gpus": 1, "steps": 1, "warmup": 3, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (random packed operands)",
+        "config": {"workload": "config1: 9 pairs x {QKV, O, gate/up, down} x M in {1,8,64,256,512}",
+                   "l2": "flushed before every call"},
+        "cpu_baseline": {"value": round(total_cpu, 1), "unit": "us", "cores": cores, "kind": "port",
+                         "sample": "every case once, the reference's dequantize-and-matmul formula"},
+        "hbm_gbs": result["hbm_gbs"], "int8_tops": result["int8_tops"], "cases": result["rows"]}), flush=True)
+
+
 def main():
     args = parse()
+    if args.config in (0, 1):
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "configs 0 and 1 report their CPU formula inside "
+                                                                 "the line's cpu_baseline"}), flush=True)
+            return
+        (config0 if args.config == 0 else config1)(args)
+        return
     if args.config == 3:
         (reference_arm3 if args.impl == "reference" else ours3)(args)
         return
