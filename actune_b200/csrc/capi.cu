@@ -335,8 +335,11 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   const int bn = wt ? pick_wt(variant, M) : pick_bn(variant, M, N, g_devices[dev].num_sms);
   CUtensorMap ta, tw;
   // Token tile: int8 rows land in the SW128 operand layout; packed sub-byte rows are
-  // staged unswizzled for the in-kernel expansion.
-  rc = encode_map(&ta, a, M, K * A / 8, A == 8 ? 128 : 16 * A, wt ? bn : 128, A == 8 ? Swz::B128 : Swz::None);
+  // staged unswizzled for the in-kernel expansion.  A single tile of few tokens loads
+  // only its rows (rounded up to 8): the TMA unit spends time on every box row,
+  // zero-filled ones included.  The persistent form keeps whole-tile boxes.
+  const int a_rows = wt ? bn : (M <= 128 && !is_persistent_variant(variant) ? (int)((M + 7) / 8 * 8) : 128);
+  rc = encode_map(&ta, a, M, K * A / 8, A == 8 ? 128 : 16 * A, a_rows, A == 8 ? Swz::B128 : Swz::None);
   if (rc != ACTUNE_OK) return rc;
   if (wt) {
     // Weight tile [128 rows x 16*W bytes] with the swizzle whose span is the row width,
@@ -359,6 +362,7 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
   p.bias_dtype = bias == nullptr ? kDtNone : bias_dtype;
   p.out_dtype = out_dtype;
   p.out_vec_ok = (N % 8 == 0) && aligned(out, 16);
+  p.a_box_rows = wt ? 0 : a_rows;
   if (!wt && dots == nullptr && is_persistent_variant(variant) && persistent_ok(out, out_dtype, N)) {
     CUtensorMap to;
     rc = encode_map(&to, out, M, N * 2, 128, 128, Swz::B128);

@@ -42,6 +42,7 @@ struct GemmParams {
   int out_vec_ok;          // N % 8 == 0 and out 16-byte aligned
   int rowwise_order;       // row-scaled modes: 0 (acc*as)*ws, 1 acc*(as*ws) (the per-row A4 native order)
   int gemv_boxes2d;        // decode: packed rows not whole 128-byte blocks, one 2-D box per block
+  int a_box_rows;          // GEMM: token box height of the activation map (0: a whole 128-row tile)
   int n_base, n_end;       // GEMM: output columns [n_base, n_end) of [0, N) (n_end 0: N)
 };
 
@@ -85,10 +86,11 @@ struct Group64Cfg {
   static constexpr int OUT_STAGE_BYTES = BM * (BN + 4) * 4;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES > OUT_STAGE_BYTES ? STAGES * STAGE_BYTES : OUT_STAGE_BYTES;
   static constexpr int SMEM_BYTES = RING_BYTES + 1024;  // + alignment slack
-  // Bytes one stage's two TMA loads deliver (full boxes; OOB parts are zero-filled).
-  static constexpr uint32_t TX_BYTES = BM * KS * A / 8 + BN * KS * W / 8;
   // int8 operand value = code * 2^(8-bits): the dot carries 2^SHIFT.
   static constexpr int SHIFT = (8 - A) + (8 - W);
+  // Bytes one stage's two TMA loads deliver with a whole 128-row token box (OOB parts
+  // of a box are zero-filled and count).
+  static constexpr uint32_t TX_BYTES = BM * KS * A / 8 + BN * KS * W / 8;
   static_assert(STAGES >= 2, "stages");
 };
 
@@ -99,8 +101,13 @@ struct Group64Cfg {
 // items; thread t handles items t, t + NT, ... which all share the same chunk
 // index and row phase (r mod 8), so every address is a per-thread base plus a
 // compile-time offset.
+//
+// Only rows below `rows_valid` are expanded: the operand rows past the last token
+// keep whatever they held, which reaches only accumulator rows that are never stored
+// (an MMA row depends on its own operand row alone).
 template <int BITS, int ROWS, int NT_ALL>
-__device__ __forceinline__ void unpack_stage(const uint8_t* __restrict__ stg, uint8_t* __restrict__ op, int tid) {
+__device__ __forceinline__ void unpack_stage(const uint8_t* __restrict__ stg, uint8_t* __restrict__ op, int tid,
+                                             int rows_valid = ROWS) {
   constexpr int IPR = BITS;                   // items per row: 16*BITS packed bytes / 16
   constexpr int CHUNKS = 8 / IPR;             // output chunks per item
   constexpr int ITEMS = ROWS * IPR;
@@ -114,8 +121,11 @@ __device__ __forceinline__ void unpack_stage(const uint8_t* __restrict__ stg, ui
   const uint8_t* src = stg + tid * 16;
   uint8_t* row = op + (r0 >> 3) * 1024 + x * 128;
   const int c0 = i * CHUNKS;
+  // Passes that hold a valid row (all of them for a full tile).
+  const int passes = rows_valid >= ROWS ? ITEMS / NT : (rows_valid - r0 + ROW_STEP - 1) / ROW_STEP;
 #pragma unroll
   for (int j = 0; j < ITEMS / NT; ++j) {
+    if (j >= passes) break;
     const uint4 v = *reinterpret_cast<const uint4*>(src + j * NT * 16);
     uint8_t* dst = row + j * (ROW_STEP / 8) * 1024;
     if constexpr (BITS == 4) {
@@ -260,6 +270,10 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
     // register of its own: an asynchronous copy reads its register operands some
     // time after issue, and rewriting one for the next copy stalls until it has.
     int issued = 0;
+    // A token box may be lower than the tile (a single tile of few tokens): the
+    // transaction count is the bytes the two boxes deliver.
+    const uint32_t tx_bytes = (uint32_t)(p.a_box_rows > 0 ? p.a_box_rows : C::BM) * (C::KS * A / 8) +
+                              (uint32_t)BN * (C::KS * W / 8);
     if (lane < 2) {
       const CUtensorMap* map = lane == 0 ? &tm_act : &tm_wgt;
       const int x_step = lane == 0 ? C::KS * A / 8 : C::KS * W / 8;
@@ -284,7 +298,7 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
           bool w_ok = true;
           if (lane == 0) {
             w_ok = mbar_wait(&empty_bar[j], ph ^ 1, kSiteProducer);
-            if (w_ok) mbar_arrive_expect_tx(&full_raw[j], C::TX_BYTES);
+            if (w_ok) mbar_arrive_expect_tx(&full_raw[j], tx_bytes);
           }
           if (!__shfl_sync(0x3u, w_ok, 0)) { ok = false; break; }
           if (j + HALF < S) xs[j + HALF] = (it0 + j + HALF) * x_step;  // read HALF copies from now
@@ -388,11 +402,12 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
     if constexpr (C::CONVERT) {
       const int ctid = threadIdx.x - 64;
       constexpr int NT = 32 * C::CVT_WARPS;
+      const int a_rows_valid = min(C::BM, p.M - m0);
       for (int it = 0; it < n_iters; ++it) {
         const int s = it % C::STAGES;
         if (!mbar_wait(&full_raw[s], (it / C::STAGES) & 1, kSiteConverter)) break;
         uint8_t* st = smem + s * C::STAGE_BYTES;
-        if constexpr (A < 8) unpack_stage<A, C::BM, NT>(st + C::OP_A_BYTES + C::OP_W_BYTES, st, ctid);
+        if constexpr (A < 8) unpack_stage<A, C::BM, NT>(st + C::OP_A_BYTES + C::OP_W_BYTES, st, ctid, a_rows_valid);
         if constexpr (W < 8)
           unpack_stage<W, BN, NT>(st + C::OP_A_BYTES + C::OP_W_BYTES + C::STG_A_BYTES, st + C::OP_A_BYTES, ctid);
         fence_proxy_async_smem();
@@ -414,10 +429,11 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
     const int m = m0 + row;
     const bool warp_live = (m0 + q * 32) < p.M;  // any valid token row in this warp
     const int col0 = n0 + e * C::COLS;
-    // TMEM is read in P parts of H columns per group: eight parts (four for narrow
-    // tiles) when converter warps share the register file, four otherwise (measured
-    // best; the part size moves the GEMM by a few percent at most).
-    constexpr int P = C::CVT_WARPS > 0 ? (C::COLS >= 64 ? 8 : C::COLS >= 16 ? 4 : 2) : (C::COLS >= 16 ? 4 : 2);
+    // TMEM is read in P parts of H columns per group: for 128-column tiles eight parts
+    // when converter warps share the register file, four otherwise; narrower tiles
+    // read a group in one or two parts (measured best; the part size moves the GEMM
+    // by a few percent at most).
+    constexpr int P = C::CVT_WARPS > 0 ? (C::COLS >= 64 ? 8 : C::COLS >= 32 ? 2 : 1) : (C::COLS >= 64 ? 4 : C::COLS >= 32 ? 2 : 1);
     constexpr int H = C::COLS / P;
     const float shift_scale = 1.0f / float(1 << C::SHIFT);
     const bool load_scales = !DOTS && warp_live && m < p.M;

@@ -257,12 +257,14 @@ def build_w4a8_bank(model, tokens, switchable=("layers.0.down_proj", "layers.1.d
     return build_bank(model, {"layers": tokens}, "w4a8", "w2a8", switchable)
 
 
-def make_oft_policy(layers=32, tokens=600, device="cuda", seed=0):
+def make_oft_policy(layers=32, tokens=600, device="cuda", seed=0, decoded=True):
     """Build the backbone, install the packed bank (frees the bf16 weights) and
-    return (model, runtime)."""
+    return (model, runtime).  ``decoded``: also keep int8 weight codes for the tile
+    GEMM (``BankRuntime.decode_weights``; bit-identical outputs)."""
     model = OFTBackbone(layers=layers, tokens=tokens, device=device, seed=seed)
     bank, clips = build_w4a8_bank(model, tokens)
     runtime = install_bank(model, bank, clips)
+    runtime.decoded_bytes = runtime.decode_weights() if decoded else 0
     torch.cuda.synchronize()
     return model, runtime
 
@@ -390,14 +392,16 @@ class Pi05Backbone(torch.nn.Module):
         return x_t + dt * v_t, time + dt
 
 
-def make_pi05_policy(device="cuda", seed=0, **shape):
+def make_pi05_policy(device="cuda", seed=0, decoded=True, **shape):
     """Build the pi0.5-shaped backbone and install its W4A4-average bank (every
-    projection of both stacks W4A4, two binary switchable matrices W4A4 / W2A4)."""
+    projection of both stacks W4A4, two binary switchable matrices W4A4 / W2A4).
+    ``decoded`` as for ``make_oft_policy``."""
     model = Pi05Backbone(device=device, seed=seed, **shape)
     tokens = {"vlm": model.prefix_tokens, "expert": model.horizon * model.steps}
     bank, clips = build_bank(model, tokens, "w4a4", "w2a4", ("vlm.0.down_proj", "expert.0.down_proj"),
                              stacks=("vlm", "expert"))
     runtime = install_bank(model, bank, clips)
+    runtime.decoded_bytes = runtime.decode_weights() if decoded else 0
     torch.cuda.synchronize()
     return model, runtime
 

@@ -111,6 +111,19 @@ def reuse_mlp_temporary(model):
     return patched
 
 
+def unpack_rows(packed, bits, k):
+    """Inverse of ``pack_rows``: int8 codes [R, k] from little-endian packed rows
+    (code j of a row sits in bits [bits*(j % per_byte), ...) of byte j // per_byte,
+    two's complement).  Install-time helper, runs where ``packed`` lives."""
+    if bits == 8:
+        return packed.view(torch.int8)[:, :k].contiguous()
+    per = 8 // bits
+    p = packed.view(torch.int8)
+    parts = [torch.bitwise_right_shift(torch.bitwise_left_shift(p, 8 - bits * (j + 1)), 8 - bits)
+             for j in range(per)]
+    return torch.stack(parts, dim=-1).reshape(p.shape[0], -1)[:, :k].contiguous()
+
+
 def pack_rows(q, bits):
     """Little-endian sub-byte packing of int8 codes [R, K] (reference grouped.py:108-111).
 
@@ -148,7 +161,19 @@ def extension():
     return _EXTENSION
 
 
+# The weight-streaming kernel (up to 32 token rows) is bound by reading the packed
+# weights, so it keeps them packed; the tile kernel above that is not, and runs
+# faster on int8 codes (no per-tile expansion of sub-byte codes).
+DECODED_MIN_TOKENS = 33
+
+
 class GroupedLinear(torch.nn.Module):
+    """``decode_weight()`` keeps, next to the packed rows, the weight codes as int8
+    bytes [N, K] (the W=8 packed form; not a buffer: the bank's storage audit counts the packed versions only).
+    Calls with more than 32 token rows then run the W=8 kernel on those codes: the
+    integer group dots are the same numbers, so outputs are bit-identical, for
+    N*K extra bytes of device memory."""
+
     def __init__(self, linear, w, a, ratios):
         super().__init__()
         self.in_features = linear.in_features
@@ -166,15 +191,39 @@ class GroupedLinear(torch.nn.Module):
             bias = bias.float()
         self.register_buffer("bias", bias)
         self.variant = _lib.VARIANT_AUTO
+        self.decoded_weight = None
+
+    def decode_weight(self):
+        """Keep the int8 weight codes for calls of more than 32 token rows (W < 8);
+        returns the bytes added.  The decoded rows are checked to pack back to the
+        stored ones."""
+        if self.w == 8 or self.decoded_weight is not None:
+            return 0
+        codes = unpack_rows(self.packed_weight, self.w, self.in_features)
+        if not torch.equal(ops.pack_rows(codes, self.w), self.packed_weight):
+            raise RuntimeError("decoded weight codes do not pack back to the stored rows")
+        self.decoded_weight = codes.view(torch.uint8)  # the W=8 packed form: one byte per code
+        return codes.numel()
+
+    def _weight_for(self, rows):
+        if self.decoded_weight is not None and rows >= DECODED_MIN_TOKENS:
+            return self.decoded_weight, 8
+        return self.packed_weight, self.w
 
     def forward(self, x):
         if not x.is_cuda:
             raise ValueError("Grouped integer backend requires CUDA")
         flat = x.reshape(-1, self.in_features).contiguous()
         packed, scales = _quantize_shared(flat, self.a)
-        out = ops.packed_linear(packed, scales, self.packed_weight, self.weight_scale, self.bias,
-                                self.in_features, self.w, self.a, out_dtype=x.dtype, variant=self.variant)
+        weight, w = self._weight_for(flat.shape[0])
+        out = ops.packed_linear(packed, scales, weight, self.weight_scale, self.bias,
+                                self.in_features, w, self.a, out_dtype=x.dtype, variant=self.variant)
         return out.reshape(*x.shape[:-1], self.out_features)
+
+
+def decode_weights(model):
+    """``decode_weight()`` on every GroupedLinear of ``model``; returns the bytes added."""
+    return sum(m.decode_weight() for m in model.modules() if isinstance(m, GroupedLinear))
 
 
 class GroupedPaddedLinear(torch.nn.Module):

@@ -69,6 +69,14 @@ class BankRuntime:
         counts = {name: module.input_elements for name, module in self.modules.items()}
         return self.bank.check_request(configuration, counts)
 
+    def decode_weights(self):
+        """Keep int8 weight codes beside every packed sub-byte version, used by calls
+        of more than 32 token rows (bit-identical outputs, faster tile GEMM); returns
+        the device bytes added.  The bank's storage accounting covers the packed
+        versions only."""
+        from .kernels.grouped import decode_weights
+        return sum(decode_weights(module) for module in self.modules.values())
+
 
 def install_bank(model, bank, clips, *, channel_scales=None, tune=False):
     """Replace every bank target of ``model`` with a ResidentLinear (all nine W/A pairs).

@@ -182,7 +182,8 @@ def cpu_sample(layers_in_sample, repeats=3, warmup=1):
 def bench_config(world, layers=LAYERS):
     """The `config` object both arms print (identical keys and values)."""
     return {"workload": WORKLOAD, "tokens": TOKENS, "layers": layers, "parallelism": f"replicas x{world}",
-            "l2": "inputs larger than L2 (3.4 GB packed weights streamed per chunk, L2 126 MB)"}
+            "l2": "inputs larger than L2 (3.4 GB of packed weights per chunk, 6.5 GB as the int8 codes the tile "
+                  "GEMM reads; L2 126 MB)"}
 
 
 def reference_arm(args):
@@ -398,8 +399,10 @@ def dominant_gemm(torch, model):
     out = torch.empty(TOKENS, 3 * HIDDEN, device="cuda", dtype=torch.bfloat16)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
+    weight, w = backend._weight_for(TOKENS)  # the int8 codes when the runtime decoded them
+
     def launch():
-        ops.packed_linear(pa, as_, backend.packed_weight, backend.weight_scale, None, HIDDEN, 4, 8, out=out)
+        ops.packed_linear(pa, as_, weight, backend.weight_scale, None, HIDDEN, w, 8, out=out)
 
     for _ in range(3):
         launch()
@@ -413,11 +416,11 @@ def dominant_gemm(torch, model):
         e.synchronize()
         times.append(s.elapsed_time(e))
     del flush
-    return statistics.median(times) * 1e-3
+    return statistics.median(times) * 1e-3, w
 
 
-def profile_traffic():
-    f = ROOT / "profiles" / "gemm_w4a8_qkv_m600.json"
+def profile_traffic(decoded):
+    f = ROOT / "profiles" / ("gemm_w4a8_decoded_qkv_m600.json" if decoded else "gemm_w4a8_qkv_m600.json")
     if f.exists():
         try:
             return json.loads(f.read_text()).get("dram_bytes_per_launch")
@@ -497,11 +500,11 @@ def ours(args):
 
     line = None
     if rank == 0:
-        gemm_s = dominant_gemm(torch, model)
+        gemm_s, gemm_w = dominant_gemm(torch, model)
         peak = int8_peak_tops(torch)
         ops_per_launch = 2 * TOKENS * HIDDEN * 3 * HIDDEN
         achieved = ops_per_launch / gemm_s / 1e12
-        traffic = profile_traffic()
+        traffic = profile_traffic(gemm_w == 8)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             secs = cpu_sample(args.cpu_sample_layers)
@@ -523,12 +526,14 @@ def ours(args):
                     "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
                          "unit": "TOP/s (int8)", "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "group64_gemm_kernel W4A8 M=600 K=4096 N=12288 (QKV)",
+                         "kernel": "group64_gemm_kernel W4A8 M=600 K=4096 N=12288 (QKV), "
+                                   + ("weight codes read as int8 (decoded copy)" if gemm_w == 8 else "packed 4-bit weights"),
                          "peak_source": "torch._int_mm int8 8192^3, measured in this run (of measured)",
                          "gemm_us": round(gemm_s * 1e6, 2)},
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "gpu_launches": launches_per_step * args.steps,
+            "decoded_weight_bytes": runtime.decoded_bytes,
         }
         print(json.dumps(line), flush=True)
     policy.release()
@@ -548,8 +553,10 @@ def dominant_gemm3(torch, model):
     out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
+    weight, w = backend._weight_for(m)
+
     def launch():
-        ops.packed_linear(pa, as_, backend.packed_weight, backend.weight_scale, None, k, 4, 4, out=out)
+        ops.packed_linear(pa, as_, weight, backend.weight_scale, None, k, w, 4, out=out)
 
     for _ in range(3):
         launch()
@@ -670,6 +677,7 @@ def ours3(args):
                          "peak_source": "torch._int_mm int8 8192^3, measured in this run (of measured)",
                          "gemm_us": round(gemm_s * 1e6, 2)},
             "cpu_baseline": cpu, "clocks": clock_info, "gpu_launches": launches * args.steps,
+            "decoded_weight_bytes": runtime.decoded_bytes,
         }
         print(json.dumps(line), flush=True)
     prefix_replay.release()
@@ -773,12 +781,13 @@ def ours4(args):
         pa, as_ = ops.quantize_group64(xq, 4)
         out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
         flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        weight, w = backend._weight_for(m)
         times = []
         for r in range(13):
             flush.zero_()
             s, e = torch.cuda.Event(True), torch.cuda.Event(True)
             s.record()
-            ops.packed_linear(pa, as_, backend.packed_weight, backend.weight_scale, None, k, 4, 4, out=out)
+            ops.packed_linear(pa, as_, weight, backend.weight_scale, None, k, w, 4, out=out)
             e.record()
             e.synchronize()
             if r >= 3:
@@ -817,6 +826,7 @@ def ours4(args):
                          "gemm_us": round(gemm_s * 1e6, 2)},
             "routing": {"switches": int(router.switches), "rounds": args.warmup + 2 * args.steps},
             "cpu_baseline": cpu, "clocks": clock_info,
+            "decoded_weight_bytes": serving.runtime.decoded_bytes,
         }
         print(json.dumps(line), flush=True)
     serving.release()
