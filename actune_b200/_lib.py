@@ -30,6 +30,7 @@ VARIANT_MAX = VARIANT_BN128P
 # Every symbol the header declares (checked by the CPU test suite).
 EXPORTS = (
     "actune_quantize_group64",
+    "actune_quantize_group64_codes",
     "actune_packed_linear",
     "actune_quantize_rows_a8",
     "actune_tokenwise_linear",
@@ -66,6 +67,7 @@ class ActuneError(RuntimeError):
 def _declare(L):
     p, i32, i64, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
     L.actune_quantize_group64.argtypes = [p, i32, i64, i64, i32, p, p, p]
+    L.actune_quantize_group64_codes.argtypes = [p, i32, i64, i64, i32, p, p, p]
     L.actune_packed_linear.argtypes = [p, p, p, p, p, i32, p, i32, i64, i64, i64, i32, i32, i32, p]
     L.actune_packed_linear_dots.argtypes = [p, p, p, i64, i64, i64, i32, i32, i32, p]
     L.actune_quantize_rows_a8.argtypes = [p, i32, i64, i64, p, p, p]

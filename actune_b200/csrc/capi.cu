@@ -502,8 +502,9 @@ const char* actune_status_string(int status) {
   }
 }
 
-int actune_quantize_group64(const void* x, int x_dtype, int64_t M, int64_t K, int A, uint8_t* packed, float* scales,
-                            void* stream) {
+namespace {
+int quantize_group64(const void* x, int x_dtype, int64_t M, int64_t K, int A, bool codes8, uint8_t* packed,
+                     float* scales, void* stream) {
   if (!valid_bits(A) || !valid_float_dtype(x_dtype) || M < 0 || K <= 0 || K % 64) return ACTUNE_ERR_INVALID_VALUE;
   if (M > 0 && (x == nullptr || packed == nullptr || scales == nullptr)) return ACTUNE_ERR_INVALID_VALUE;
   int dev = 0;
@@ -512,9 +513,20 @@ int actune_quantize_group64(const void* x, int x_dtype, int64_t M, int64_t K, in
   if (M == 0) return ACTUNE_OK;
   if (!aligned(x, 16) || !aligned(packed, 8) || !aligned(scales, 4)) return ACTUNE_ERR_MISALIGNED;
   const int dt = x_dtype == ACTUNE_DTYPE_BF16 ? kDtBF16 : (x_dtype == ACTUNE_DTYPE_F16 ? kDtF16 : kDtF32);
-  cudaError_t e = launch_quantize_group64(x, dt, M * (K / 64), A, packed, scales, g_devices[dev].num_sms,
+  cudaError_t e = launch_quantize_group64(x, dt, M * (K / 64), A, codes8, packed, scales, g_devices[dev].num_sms,
                                           reinterpret_cast<cudaStream_t>(stream));
   return cuda_status(e);
+}
+}  // namespace
+
+int actune_quantize_group64(const void* x, int x_dtype, int64_t M, int64_t K, int A, uint8_t* packed, float* scales,
+                            void* stream) {
+  return quantize_group64(x, x_dtype, M, K, A, false, packed, scales, stream);
+}
+
+int actune_quantize_group64_codes(const void* x, int x_dtype, int64_t M, int64_t K, int A, uint8_t* codes,
+                                  float* scales, void* stream) {
+  return quantize_group64(x, x_dtype, M, K, A, true, codes, scales, stream);
 }
 
 int actune_packed_linear(const uint8_t* a, const float* a_scale, const uint8_t* w, const float* w_scale,

@@ -349,13 +349,16 @@ __device__ __forceinline__ uint2 unpack_w4_word(uint32_t x) {
 // lanes must call it together).  Restates actune/kernels/grouped.py:55-71:
 //   scale = max(absmax, 1e-8) / (2^(A-1) - 1)               IEEE division
 //   code  = clamp(rint(x / scale), -2^(A-1), 2^(A-1) - 1)    IEEE division, RNE
-// and packs the lane's 8 codes little-endian, code i at bit i*A of `word`.
-// Returns the group's scale (the same in all 8 lanes).
-template <int A>
+// and packs the lane's 8 codes little-endian, code i at bit i*OUT of `word`: the
+// A-bit packed layout (OUT = A) or one int8 per code (OUT = 8, the layout the
+// W=8 / A=8 GEMM reads, whatever A).  Returns the group's scale (the same in all 8
+// lanes).
+template <int A, int OUT = A>
 __device__ __forceinline__ float quantize_lane8(const float (&v)[8], uint32_t (&word)[2]) {
   constexpr float kPositive = float((1 << (A - 1)) - 1);
   constexpr float kLo = -float(1 << (A - 1));
-  constexpr int kMask = (1 << A) - 1;
+  static_assert(OUT == A || OUT == 8, "codes are stored at A bits or as int8");
+  constexpr int kMask = (1 << OUT) - 1;
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -369,7 +372,7 @@ __device__ __forceinline__ float quantize_lane8(const float (&v)[8], uint32_t (&
     float q = rintf(__fdiv_rn(v[i], scale));
     q = fminf(fmaxf(q, kLo), kPositive);
     const uint32_t field = (uint32_t)((int)q) & kMask;
-    const int bit = i * A;
+    const int bit = i * OUT;
     word[bit >> 5] |= field << (bit & 31);
   }
   return scale;

@@ -125,8 +125,9 @@ __device__ __forceinline__ float bf16_round(float v) { return bf2f(__float2bfloa
 // One CTA (256 threads) per row, CPT chunks of 8 elements per thread kept in
 // registers: D <= 2048 * CPT, D % 8 == 0.  Same arithmetic as rmsnorm_kernel.
 // QA > 0: the bf16 output is also quantized (group 64, QA bits) into qpacked /
-// qscales, from the rounded values it stores (D % 256 == 0: whole warps per row).
-template <int CPT, int QA>
+// qscales, from the rounded values it stores (D % 256 == 0: whole warps per row);
+// QOUT = QA packs the codes, QOUT = 8 stores one int8 code per element.
+template <int CPT, int QA, int QOUT = QA>
 __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const __nv_bfloat16* __restrict__ x,
                                                           const __nv_bfloat16* __restrict__ residual,
                                                           const __nv_bfloat16* __restrict__ weight,
@@ -180,8 +181,8 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const __nv_bfloat16* _
         float q[8];
         unpack8(stored, q);
         uint32_t word[2];
-        const float scale = actune::quantize_lane8<QA>(q, word);
-        actune::store_lane_codes<QA>(qpacked + (base + i) * QA / 8, word);
+        const float scale = actune::quantize_lane8<QA, QOUT>(q, word);
+        actune::store_lane_codes<QOUT>(qpacked + (base + i) * QOUT / 8, word);
         if ((threadIdx.x & 7) == 0) qscales[(base + i) / 64] = scale;
       }
     }
@@ -219,10 +220,10 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(__nv_bfloat16* __restrict
 }
 
 // Gated activation, 8 outputs per thread (I % 8 == 0).  QA > 0: the output is also
-// quantized (group 64, QA bits; I % 64 == 0) from the rounded values it stores.
-// Warps step through the items together so that each 64-group's 8 lanes shuffle
-// as one segment.
-template <int QA>
+// quantized (group 64, QA bits; I % 64 == 0) from the rounded values it stores,
+// packed (QOUT = QA) or one int8 code per element (QOUT = 8).  Warps step through
+// the items together so that each 64-group's 8 lanes shuffle as one segment.
+template <int QA, int QOUT = QA>
 __global__ void __launch_bounds__(256) gated_act_vec_kernel(const __nv_bfloat16* __restrict__ gu,
                                                             __nv_bfloat16* __restrict__ out, int T, int I, int gelu,
                                                             uint8_t* __restrict__ qpacked,
@@ -259,9 +260,9 @@ __global__ void __launch_bounds__(256) gated_act_vec_kernel(const __nv_bfloat16*
       float q[8];
       unpack8(stored, q);
       uint32_t word[2];
-      const float scale = actune::quantize_lane8<QA>(q, word);
+      const float scale = actune::quantize_lane8<QA, QOUT>(q, word);
       if (live) {
-        actune::store_lane_codes<QA>(qpacked + item * QA, word);
+        actune::store_lane_codes<QOUT>(qpacked + item * QOUT, word);
         if ((lane & 7) == 0) qscales[item / 8] = scale;
       }
     }
@@ -276,13 +277,16 @@ int grid_for(int64_t n) {
   return (int)(b < 1 ? 1 : b);
 }
 
-template <int QA>
+template <int QA, int QOUT = QA>
 cudaError_t launch_rmsnorm_q(const __nv_bfloat16* xb, const __nv_bfloat16* rb, const __nv_bfloat16* wb,
                              __nv_bfloat16* ob, __nv_bfloat16* rob, int64_t T, int64_t D, float eps, int gemma,
                              uint8_t* qp, float* qs, cudaStream_t cs) {
-  if (D <= 2048) rmsnorm_vec_kernel<1, QA><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
-  else if (D <= 4096) rmsnorm_vec_kernel<2, QA><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
-  else rmsnorm_vec_kernel<4, QA><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
+  if (D <= 2048)
+    rmsnorm_vec_kernel<1, QA, QOUT><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
+  else if (D <= 4096)
+    rmsnorm_vec_kernel<2, QA, QOUT><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
+  else
+    rmsnorm_vec_kernel<4, QA, QOUT><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
   return cudaGetLastError();
 }
 
@@ -348,8 +352,8 @@ int actune_harness_gated_act(const void* gu, void* out, int64_t T, int64_t I, in
 }
 
 int actune_harness_rmsnorm_q(const void* x, const void* residual, const void* weight, void* out, void* residual_out,
-                             int64_t T, int64_t D, float eps, int gemma, int A, uint8_t* packed, float* scales,
-                             void* stream) {
+                             int64_t T, int64_t D, float eps, int gemma, int A, int codes8, uint8_t* packed,
+                             float* scales, void* stream) {
   if (T < 0 || D <= 0 || D > 8192 || D % 256 || x == nullptr || weight == nullptr || out == nullptr ||
       packed == nullptr || scales == nullptr || (residual != nullptr && residual_out == nullptr) ||
       (A != 2 && A != 4 && A != 8))
@@ -365,13 +369,15 @@ int actune_harness_rmsnorm_q(const void* x, const void* residual, const void* we
   auto* rob = reinterpret_cast<__nv_bfloat16*>(residual_out);
   auto* cs = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e = A == 8 ? launch_rmsnorm_q<8>(xb, rb, wb, ob, rob, T, D, eps, gemma, packed, scales, cs)
-                : A == 4 ? launch_rmsnorm_q<4>(xb, rb, wb, ob, rob, T, D, eps, gemma, packed, scales, cs)
-                         : launch_rmsnorm_q<2>(xb, rb, wb, ob, rob, T, D, eps, gemma, packed, scales, cs);
+                : A == 4 ? (codes8 ? launch_rmsnorm_q<4, 8>(xb, rb, wb, ob, rob, T, D, eps, gemma, packed, scales, cs)
+                                   : launch_rmsnorm_q<4>(xb, rb, wb, ob, rob, T, D, eps, gemma, packed, scales, cs))
+                         : (codes8 ? launch_rmsnorm_q<2, 8>(xb, rb, wb, ob, rob, T, D, eps, gemma, packed, scales, cs)
+                                   : launch_rmsnorm_q<2>(xb, rb, wb, ob, rob, T, D, eps, gemma, packed, scales, cs));
   return e == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
 }
 
-int actune_harness_gated_act_q(const void* gu, void* out, int64_t T, int64_t I, int gelu, int A, uint8_t* packed,
-                               float* scales, void* stream) {
+int actune_harness_gated_act_q(const void* gu, void* out, int64_t T, int64_t I, int gelu, int A, int codes8,
+                               uint8_t* packed, float* scales, void* stream) {
   if (T < 0 || I <= 0 || I % 64 || gu == nullptr || out == nullptr || packed == nullptr || scales == nullptr ||
       (A != 2 && A != 4 && A != 8))
     return ACTUNE_ERR_INVALID_VALUE;
@@ -382,7 +388,9 @@ int actune_harness_gated_act_q(const void* gu, void* out, int64_t T, int64_t I, 
   auto* cs = reinterpret_cast<cudaStream_t>(stream);
   const int grid = grid_for(T * I / 8);
   if (A == 8) gated_act_vec_kernel<8><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
+  else if (A == 4 && codes8) gated_act_vec_kernel<4, 8><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
   else if (A == 4) gated_act_vec_kernel<4><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
+  else if (codes8) gated_act_vec_kernel<2, 8><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
   else gated_act_vec_kernel<2><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
   return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
 }

@@ -10,8 +10,9 @@ namespace actune {
 // A4 (bits 4: packed [M, K/2]) backends (K % 8 == 0, 16-byte aligned x).
 cudaError_t launch_quantize_rows(const void* x, int dtype, int64_t M, int64_t K, int bits, uint8_t* codes,
                                  float* scales, cudaStream_t stream);
-cudaError_t launch_quantize_group64(const void* x, int dtype, int64_t groups, int A, uint8_t* packed, float* scales,
-                                    int num_sms, cudaStream_t stream);
+// codes8: one int8 code per element instead of packed A-bit codes.
+cudaError_t launch_quantize_group64(const void* x, int dtype, int64_t groups, int A, bool codes8, uint8_t* packed,
+                                    float* scales, int num_sms, cudaStream_t stream);
 cudaError_t launch_weight_codes(const void* w, int dtype, int64_t N, int64_t K, int W, int A, const float* clip,
                                 int8_t* codes, float* scale, cudaStream_t stream);
 cudaError_t launch_r4_refine(const void* w, int dtype, int64_t N, int64_t K, const int8_t* q4, const float* scale4,

@@ -55,7 +55,9 @@ __device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
   v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-template <int A, typename T>
+// OUT = A: packed A-bit codes [groups * 64 * A / 8]; OUT = 8: one int8 code per
+// element (the same A-bit codes, for the W=8 / A=8 GEMM).
+template <int A, typename T, int OUT = A>
 __global__ void __launch_bounds__(256) quantize_group64_kernel(const T* __restrict__ x, uint8_t* __restrict__ packed,
                                                                float* __restrict__ scales, int64_t groups) {
   const int lane = threadIdx.x & 31;
@@ -73,9 +75,9 @@ __global__ void __launch_bounds__(256) quantize_group64_kernel(const T* __restri
       for (int i = 0; i < 8; ++i) v[i] = 0.f;
     }
     uint32_t word[2];
-    const float scale = quantize_lane8<A>(v, word);
+    const float scale = quantize_lane8<A, OUT>(v, word);
     if (!live) continue;
-    store_lane_codes<A>(packed + g * (64 * A / 8) + l8 * A, word);
+    store_lane_codes<OUT>(packed + g * (64 * OUT / 8) + l8 * OUT, word);
     if (l8 == 0) scales[g] = scale;
   }
 }
@@ -200,7 +202,7 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const int8_t* __restrict
 // Host launchers
 // ---------------------------------------------------------------------------
 template <typename T>
-static cudaError_t launch_quantize_t(const T* x, int64_t groups, int A, uint8_t* packed, float* scales,
+static cudaError_t launch_quantize_t(const T* x, int64_t groups, int A, bool codes8, uint8_t* packed, float* scales,
                                      int num_sms, cudaStream_t stream) {
   const int threads = 256;
   const int64_t warps_needed = (groups + 3) / 4;
@@ -208,24 +210,30 @@ static cudaError_t launch_quantize_t(const T* x, int64_t groups, int A, uint8_t*
   const int64_t cap = (int64_t)num_sms * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  switch (A) {
-    case 2: quantize_group64_kernel<2, T><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups); break;
-    case 4: quantize_group64_kernel<4, T><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups); break;
-    default: quantize_group64_kernel<8, T><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups); break;
-  }
+  if (codes8 && A == 2)
+    quantize_group64_kernel<2, T, 8><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups);
+  else if (codes8 && A == 4)
+    quantize_group64_kernel<4, T, 8><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups);
+  else if (A == 2)
+    quantize_group64_kernel<2, T><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups);
+  else if (A == 4)
+    quantize_group64_kernel<4, T><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups);
+  else
+    quantize_group64_kernel<8, T><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups);
   return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_group64(const void* x, int dtype, int64_t groups, int A, uint8_t* packed, float* scales,
-                                    int num_sms, cudaStream_t stream) {
+cudaError_t launch_quantize_group64(const void* x, int dtype, int64_t groups, int A, bool codes8, uint8_t* packed,
+                                    float* scales, int num_sms, cudaStream_t stream) {
   if (groups == 0) return cudaSuccess;
   switch (dtype) {
     case kDtBF16:
-      return launch_quantize_t(reinterpret_cast<const __nv_bfloat16*>(x), groups, A, packed, scales, num_sms, stream);
+      return launch_quantize_t(reinterpret_cast<const __nv_bfloat16*>(x), groups, A, codes8, packed, scales, num_sms,
+                               stream);
     case kDtF16:
-      return launch_quantize_t(reinterpret_cast<const __half*>(x), groups, A, packed, scales, num_sms, stream);
+      return launch_quantize_t(reinterpret_cast<const __half*>(x), groups, A, codes8, packed, scales, num_sms, stream);
     default:
-      return launch_quantize_t(reinterpret_cast<const float*>(x), groups, A, packed, scales, num_sms, stream);
+      return launch_quantize_t(reinterpret_cast<const float*>(x), groups, A, codes8, packed, scales, num_sms, stream);
   }
 }
 

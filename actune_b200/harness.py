@@ -45,9 +45,9 @@ def _hlib():
         L.actune_harness_rope.restype = i32
         L.actune_harness_gated_act.argtypes = [p, p, i64, i64, i32, p]
         L.actune_harness_gated_act.restype = i32
-        L.actune_harness_rmsnorm_q.argtypes = [p, p, p, p, p, i64, i64, ctypes.c_float, i32, i32, p, p, p]
+        L.actune_harness_rmsnorm_q.argtypes = [p, p, p, p, p, i64, i64, ctypes.c_float, i32, i32, i32, p, p, p]
         L.actune_harness_rmsnorm_q.restype = i32
-        L.actune_harness_gated_act_q.argtypes = [p, p, i64, i64, i32, i32, p, p, p]
+        L.actune_harness_gated_act_q.argtypes = [p, p, i64, i64, i32, i32, i32, p, p, p]
         L.actune_harness_gated_act_q.restype = i32
         _H = L
     return _H
@@ -61,23 +61,26 @@ def _s(t):
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
 
 
-def rmsnorm(x, weight, eps, residual=None, gemma=False, quant_bits=None):
+def rmsnorm(x, weight, eps, residual=None, gemma=False, quant_bits=None, codes8=False):
     """(normed, new_residual): fused residual add + RMSNorm over the last dim.
 
-    With ``quant_bits`` the kernel also writes the group-64 packed activations of
-    the normed output and offers them to the active shared activation scope, so
-    the next projection does not launch its own quantizer."""
+    With ``quant_bits`` the kernel also writes the group-64 activations of the
+    normed output (packed, or one int8 code each with ``codes8``) and offers them
+    to the active shared activation scope, so the next projection does not launch
+    its own quantizer."""
     x = x.contiguous()
     out = torch.empty_like(x)
     res_out = torch.empty_like(x) if residual is not None else None
     T, D = x.numel() // x.shape[-1], x.shape[-1]
     if quant_bits and D % 256 == 0 and D <= 8192:
-        packed = torch.empty((T, D * quant_bits // 8), device=x.device, dtype=torch.uint8)
+        width = 8 if codes8 else quant_bits
+        packed = torch.empty((T, D * width // 8), device=x.device, dtype=torch.uint8)
         scales = torch.empty((T, D // 64), device=x.device, dtype=torch.float32)
         _lib.check(_hlib().actune_harness_rmsnorm_q(_p(x), _p(residual), _p(weight), _p(out), _p(res_out), T, D,
-                                                     float(eps), 1 if gemma else 0, int(quant_bits), _p(packed),
+                                                     float(eps), 1 if gemma else 0, int(quant_bits),
+                                                     1 if codes8 else 0, _p(packed),
                                                      _p(scales), _s(x)), "rmsnorm")
-        share_quantized(out.view(T, D), quant_bits, packed, scales)
+        share_quantized(out.view(T, D), quant_bits, packed, scales, codes8)
     else:
         _lib.check(_hlib().actune_harness_rmsnorm(_p(x), _p(residual), _p(weight), _p(out), _p(res_out), T, D,
                                                    float(eps), 1 if gemma else 0, _s(x)), "rmsnorm")
@@ -90,33 +93,38 @@ def rope_(qkv, cos, sin, hq, hkv, dh):
     return qkv
 
 
-def gated_act(gu, gelu=False, quant_bits=None):
-    """act(gate) * up for gu = [gate | up]; with ``quant_bits`` also the packed
-    group-64 activations of the result, offered to the shared activation scope."""
+def gated_act(gu, gelu=False, quant_bits=None, codes8=False):
+    """act(gate) * up for gu = [gate | up]; with ``quant_bits`` also the group-64
+    activations of the result (packed, or int8 codes with ``codes8``), offered to
+    the shared activation scope."""
     I = gu.shape[-1] // 2
     T = gu.numel() // gu.shape[-1]
     gu = gu.contiguous()
     out = torch.empty(*gu.shape[:-1], I, device=gu.device, dtype=gu.dtype)
     if quant_bits and I % 64 == 0:
-        packed = torch.empty((T, I * quant_bits // 8), device=gu.device, dtype=torch.uint8)
+        width = 8 if codes8 else quant_bits
+        packed = torch.empty((T, I * width // 8), device=gu.device, dtype=torch.uint8)
         scales = torch.empty((T, I // 64), device=gu.device, dtype=torch.float32)
         _lib.check(_hlib().actune_harness_gated_act_q(_p(gu), _p(out), T, I, 1 if gelu else 0, int(quant_bits),
-                                                       _p(packed), _p(scales), _s(gu)), "gated_act")
-        share_quantized(out.view(T, I), quant_bits, packed, scales)
+                                                       1 if codes8 else 0, _p(packed), _p(scales), _s(gu)),
+                   "gated_act")
+        share_quantized(out.view(T, I), quant_bits, packed, scales, codes8)
     else:
         _lib.check(_hlib().actune_harness_gated_act(_p(gu), _p(out), T, I, 1 if gelu else 0, _s(gu)), "gated_act")
     return out
 
 
-def input_bits(module):
-    """The activation width `module` quantizes its input with, when the input
-    reaches its quantizer unchanged (a grouped bank module without K padding or a
-    runtime channel scale, inside an active shared activation scope); else None."""
+def input_format(module, rows):
+    """{"quant_bits": A, "codes8": bool}: how `module` quantizes an input of `rows`
+    token rows, when the input reaches its quantizer unchanged (a grouped bank
+    module without K padding or a runtime channel scale, inside an active shared
+    activation scope); else {} (the glue then writes no activations)."""
     if not shared_activation_active() or not hasattr(module, "active_backend"):
-        return None
+        return {}
     if getattr(module, "padding", 0) or getattr(module, "input_scale", None) is not None:
-        return None
-    return module.active_backend().a
+        return {}
+    bits, codes8 = module.active_backend().activation_format(rows)
+    return {"quant_bits": bits, "codes8": codes8}
 
 
 def rope_tables(T, dh, theta, device):
@@ -154,7 +162,8 @@ class DecoderLayer(torch.nn.Module):
         [0, offset + T) -- the prefix cached by earlier calls plus this call."""
         rows = x.shape[0]
         B, T = batch, rows // batch
-        h, residual = rmsnorm(x, self.input_norm, self.eps, residual, self.gemma, input_bits(self.qkv_proj))
+        h, residual = rmsnorm(x, self.input_norm, self.eps, residual, self.gemma,
+                              **input_format(self.qkv_proj, rows))
         qkv = self.qkv_proj(h)
         rope_(qkv, cos, sin, self.heads, self.kv_heads, self.head_dim)
         qd, kvd = self.heads * self.head_dim, self.kv_heads * self.head_dim
@@ -172,8 +181,9 @@ class DecoderLayer(torch.nn.Module):
                                               enable_gqa=self.kv_heads != self.heads)
         attn = attn.transpose(1, 2).reshape(rows, self.heads * self.head_dim)
         x = self.o_proj(attn)
-        h, residual = rmsnorm(x, self.post_norm, self.eps, residual, self.gemma, input_bits(self.gate_up_proj))
-        x = self.down_proj(gated_act(self.gate_up_proj(h), gelu=self.gemma, quant_bits=input_bits(self.down_proj)))
+        h, residual = rmsnorm(x, self.post_norm, self.eps, residual, self.gemma,
+                              **input_format(self.gate_up_proj, rows))
+        x = self.down_proj(gated_act(self.gate_up_proj(h), gelu=self.gemma, **input_format(self.down_proj, rows)))
         return x, residual
 
 

@@ -60,29 +60,30 @@ def shared_activation_active():
     return _SHARED.get() is not None
 
 
-def share_quantized(flat, bits, packed, scales):
-    """Offer already packed activations of `flat` (bit-identical to what
-    ``ops.quantize_group64(flat, bits)`` returns) to the active shared activation
-    scope, so the next projection reading `flat` reuses them.  No-op outside one."""
+def share_quantized(flat, bits, packed, scales, codes8=False):
+    """Offer already quantized activations of `flat` (bit-identical to what
+    ``ops.quantize_group64(flat, bits, codes8=codes8)`` returns) to the active shared
+    activation scope, so the next projection reading `flat` reuses them.  No-op
+    outside one."""
     cache = _SHARED.get()
     if cache is None:
         return False
-    key = (flat.data_ptr(), _version(flat), tuple(flat.shape), flat.dtype, flat.device, bits)
+    key = (flat.data_ptr(), _version(flat), tuple(flat.shape), flat.dtype, flat.device, bits, bool(codes8))
     cache.append((key, flat, packed, scales))
     if len(cache) > _SHARED_CAPACITY:
         cache.pop(0)
     return True
 
 
-def _quantize_shared(flat, bits):
+def _quantize_shared(flat, bits, codes8=False):
     cache = _SHARED.get()
     if cache is None:
-        return ops.quantize_group64(flat, bits)
-    key = (flat.data_ptr(), _version(flat), tuple(flat.shape), flat.dtype, flat.device, bits)
+        return ops.quantize_group64(flat, bits, codes8=codes8)
+    key = (flat.data_ptr(), _version(flat), tuple(flat.shape), flat.dtype, flat.device, bits, bool(codes8))
     for entry_key, _, packed, scales in cache:
         if entry_key == key:
             return packed, scales
-    packed, scales = ops.quantize_group64(flat, bits)
+    packed, scales = ops.quantize_group64(flat, bits, codes8=codes8)
     cache.append((key, flat, packed, scales))
     if len(cache) > _SHARED_CAPACITY:
         cache.pop(0)
@@ -169,10 +170,11 @@ DECODED_MIN_TOKENS = 33
 
 class GroupedLinear(torch.nn.Module):
     """``decode_weight()`` keeps, next to the packed rows, the weight codes as int8
-    bytes [N, K] (the W=8 packed form; not a buffer: the bank's storage audit counts the packed versions only).
-    Calls with more than 32 token rows then run the W=8 kernel on those codes: the
-    integer group dots are the same numbers, so outputs are bit-identical, for
-    N*K extra bytes of device memory."""
+    bytes [N, K] (the W=8 packed form; not a buffer: the bank's storage audit counts
+    the packed versions only).  Calls with more than 32 token rows then quantize
+    their activations to the same A-bit codes written one byte each and run the
+    W=8 / A=8 kernel: the integer group dots and the scales are the same numbers,
+    so outputs are bit-identical, for N*K extra bytes of device memory."""
 
     def __init__(self, linear, w, a, ratios):
         super().__init__()
@@ -205,19 +207,30 @@ class GroupedLinear(torch.nn.Module):
         self.decoded_weight = codes.view(torch.uint8)  # the W=8 packed form: one byte per code
         return codes.numel()
 
-    def _weight_for(self, rows):
-        if self.decoded_weight is not None and rows >= DECODED_MIN_TOKENS:
-            return self.decoded_weight, 8
-        return self.packed_weight, self.w
+    def decoded_path(self, rows):
+        """True when a call of `rows` token rows runs on the decoded codes."""
+        return self.decoded_weight is not None and rows >= DECODED_MIN_TOKENS
+
+    def activation_format(self, rows):
+        """(bits, codes8): the quantization of a call's activations (``codes8``: the
+        A-bit codes one byte each)."""
+        return self.a, self.decoded_path(rows) and self.a < 8
+
+    def operands(self, rows):
+        """(weight, W, A) the kernel of a call of `rows` token rows runs with."""
+        if self.decoded_path(rows):
+            return self.decoded_weight, 8, 8
+        return self.packed_weight, self.w, self.a
 
     def forward(self, x):
         if not x.is_cuda:
             raise ValueError("Grouped integer backend requires CUDA")
         flat = x.reshape(-1, self.in_features).contiguous()
-        packed, scales = _quantize_shared(flat, self.a)
-        weight, w = self._weight_for(flat.shape[0])
-        out = ops.packed_linear(packed, scales, weight, self.weight_scale, self.bias,
-                                self.in_features, w, self.a, out_dtype=x.dtype, variant=self.variant)
+        rows = flat.shape[0]
+        acts, scales = _quantize_shared(flat, *self.activation_format(rows))
+        weight, w, a = self.operands(rows)
+        out = ops.packed_linear(acts, scales, weight, self.weight_scale, self.bias,
+                                self.in_features, w, a, out_dtype=x.dtype, variant=self.variant)
         return out.reshape(*x.shape[:-1], self.out_features)
 
 

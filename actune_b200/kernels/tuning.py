@@ -68,15 +68,16 @@ def grouped_forward(self, x):
     flat = x.reshape(-1, self.in_features).contiguous()
     m, k = flat.shape
     n = self.out_features
-    packed, scales = ops.quantize_group64(flat, self.a)
-    weight, w = self._weight_for(m)
+    bits, codes8 = self.activation_format(m)
+    packed, scales = ops.quantize_group64(flat, bits, codes8=codes8)
+    weight, w, a = self.operands(m)
 
     def launch(variant):
-        return ops.packed_linear(packed, scales, weight, self.weight_scale, self.bias, k, w, self.a,
+        return ops.packed_linear(packed, scales, weight, self.weight_scale, self.bias, k, w, a,
                                  out_dtype=x.dtype, variant=variant)
 
     configs = [_lib.VARIANT_AUTO, _lib.VARIANT_BN32, _lib.VARIANT_BN64, _lib.VARIANT_BN128,
                _lib.VARIANT_BN32X2, _lib.VARIANT_BN64X2, _lib.VARIANT_BN128X2,
                _lib.VARIANT_BN64P, _lib.VARIANT_BN128P]
-    key = ("grouped", w, self.a, m, k, n, str(x.dtype), self.bias is not None)
+    key = ("grouped", w, a, m, k, n, str(x.dtype), self.bias is not None)
     return launch(select(key, launch, configs, _lib.VARIANT_AUTO)).reshape(*x.shape[:-1], n)

@@ -50,20 +50,23 @@ def _cuda_contig(*tensors):
 
 
 def quantize_group64(x: torch.Tensor, bits: int, packed: torch.Tensor | None = None,
-                     scales: torch.Tensor | None = None):
-    """Group-64 activation quantizer: x [M, K] -> (packed u8 [M, K*bits/8], scales f32 [M, K/64])."""
+                     scales: torch.Tensor | None = None, codes8: bool = False):
+    """Group-64 activation quantizer: x [M, K] -> (packed u8 [M, K*bits/8], scales f32 [M, K/64]).
+    ``codes8``: the same codes one byte each, u8 [M, K] (the A=8 operand layout)."""
     _require(x.dim() == 2, "x must be 2-D [M, K]")
     m, k = x.shape
     _require(bits in (2, 4, 8), "Unsupported integer width")
     _require(k % 64 == 0, "K must be a multiple of 64")
+    width = 8 if codes8 else bits
     if packed is None:
-        packed = torch.empty((m, k * bits // 8), device=x.device, dtype=torch.uint8)
+        packed = torch.empty((m, k * width // 8), device=x.device, dtype=torch.uint8)
     if scales is None:
         scales = torch.empty((m, k // 64), device=x.device, dtype=torch.float32)
     dev = _cuda_contig(x, packed, scales)
+    entry = _lib.lib().actune_quantize_group64_codes if codes8 else _lib.lib().actune_quantize_group64
     with torch.cuda.device(dev):
-        _lib.check(_lib.lib().actune_quantize_group64(_ptr(x), dtype_code(x.dtype), m, k, bits, _ptr(packed),
-                                                      _ptr(scales), _stream(dev)), "quantize_group64")
+        _lib.check(entry(_ptr(x), dtype_code(x.dtype), m, k, bits, _ptr(packed), _ptr(scales), _stream(dev)),
+                   "quantize_group64")
     return packed, scales
 
 

@@ -395,14 +395,15 @@ def dominant_gemm(torch, model):
     layer = model.layers[0].qkv_proj  # ResidentLinear
     backend = layer.backends["w4a8"]
     x = torch.randn(TOKENS, HIDDEN, device="cuda").bfloat16()
-    pa, as_ = ops.quantize_group64(x, 8)
+    bits, codes8 = backend.activation_format(TOKENS)
+    pa, as_ = ops.quantize_group64(x, bits, codes8=codes8)
     out = torch.empty(TOKENS, 3 * HIDDEN, device="cuda", dtype=torch.bfloat16)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
-    weight, w = backend._weight_for(TOKENS)  # the int8 codes when the runtime decoded them
+    weight, w, a = backend.operands(TOKENS)  # the int8 codes when the runtime decoded them
 
     def launch():
-        ops.packed_linear(pa, as_, weight, backend.weight_scale, None, HIDDEN, w, 8, out=out)
+        ops.packed_linear(pa, as_, weight, backend.weight_scale, None, HIDDEN, w, a, out=out)
 
     for _ in range(3):
         launch()
@@ -549,14 +550,15 @@ def dominant_gemm3(torch, model):
     backend = model.vlm[0].gate_up_proj.backends["w4a4"]
     k, n, m = P3["vlm_hidden"], 2 * P3["vlm_mlp"], P3["prefix"]
     x = torch.randn(m, k, device="cuda").bfloat16()
-    pa, as_ = ops.quantize_group64(x, 4)
+    bits, codes8 = backend.activation_format(m)
+    pa, as_ = ops.quantize_group64(x, bits, codes8=codes8)
     out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
-    weight, w = backend._weight_for(m)
+    weight, w, a = backend.operands(m)
 
     def launch():
-        ops.packed_linear(pa, as_, weight, backend.weight_scale, None, k, w, 4, out=out)
+        ops.packed_linear(pa, as_, weight, backend.weight_scale, None, k, w, a, out=out)
 
     for _ in range(3):
         launch()
@@ -673,7 +675,10 @@ def ours3(args):
                     "d2h_bytes_per_step": host_out.numel() * 4},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
                          "unit": "TOP/s (int8)", "frac": round(achieved / peak, 4), "traffic": None,
-                         "kernel": "group64_gemm_kernel W4A4 M=304 K=2048 N=32768 (VLM gate/up)",
+                         "kernel": "group64_gemm_kernel W4A4 M=304 K=2048 N=32768 (VLM gate/up)"
+                                   + (", codes read as int8 (decoded weights and activations)"
+                                      if model.vlm[0].gate_up_proj.backends["w4a4"].decoded_path(P3["prefix"])
+                                      else ""),
                          "peak_source": "torch._int_mm int8 8192^3, measured in this run (of measured)",
                          "gemm_us": round(gemm_s * 1e6, 2)},
             "cpu_baseline": cpu, "clocks": clock_info, "gpu_launches": launches * args.steps,
@@ -778,16 +783,17 @@ def ours4(args):
         backend = serving.model.vlm[0].gate_up_proj.backends["w4a4"]
         m, k, n = ENVS4 * P3["prefix"], P3["vlm_hidden"], 2 * P3["vlm_mlp"]
         xq = torch.randn(m, k, device="cuda").bfloat16()
-        pa, as_ = ops.quantize_group64(xq, 4)
+        bits, codes8 = backend.activation_format(m)
+        pa, as_ = ops.quantize_group64(xq, bits, codes8=codes8)
         out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
         flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-        weight, w = backend._weight_for(m)
+        weight, w, a = backend.operands(m)
         times = []
         for r in range(13):
             flush.zero_()
             s, e = torch.cuda.Event(True), torch.cuda.Event(True)
             s.record()
-            ops.packed_linear(pa, as_, weight, backend.weight_scale, None, k, w, 4, out=out)
+            ops.packed_linear(pa, as_, weight, backend.weight_scale, None, k, w, a, out=out)
             e.record()
             e.synchronize()
             if r >= 3:
@@ -821,7 +827,9 @@ def ours4(args):
                     "d2h_bytes_per_step": ENVS4 * P3["horizon"] * P3["action_dim"] * 4},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
                          "unit": "TOP/s (int8)", "frac": round(achieved / peak, 4), "traffic": None,
-                         "kernel": f"group64_gemm_kernel W4A4 M={m} K={k} N={n} (VLM gate/up, 16 environments)",
+                         "kernel": f"group64_gemm_kernel W4A4 M={m} K={k} N={n} (VLM gate/up, 16 environments)"
+                                   + (", codes read as int8 (decoded weights and activations)"
+                                      if backend.decoded_path(m) else ""),
                          "peak_source": "torch._int_mm int8 8192^3, measured in this run (of measured)",
                          "gemm_us": round(gemm_s * 1e6, 2)},
             "routing": {"switches": int(router.switches), "rounds": args.warmup + 2 * args.steps},

@@ -87,6 +87,15 @@ typedef enum actune_variant {
 int actune_quantize_group64(const void* x, int x_dtype, int64_t M, int64_t K, int A, uint8_t* packed, float* scales,
                             void* stream);
 
+/* The same A-bit quantization written as one int8 code per element (codes: [M, K],
+ * 8-byte aligned), i.e. the W=8 / A=8 operand layout: actune_packed_linear with
+ * A = 8 on these codes and W = 8 on int8 weight codes gives bit-for-bit the output
+ * of the A-bit (and W-bit) packed call, since the integer group dots and scales are
+ * the same.  No reference counterpart (a host that keeps decoded weight codes for
+ * calls of many token rows pairs them with these). */
+int actune_quantize_group64_codes(const void* x, int x_dtype, int64_t M, int64_t K, int A, uint8_t* codes,
+                                  float* scales, void* stream);
+
 /* The packed-integer linear: out = ws * sum_g(float(dot_g) * as[:, g]) (+ bias).
  * Replaces the native op `linear(a, as, w, ws, bias, source, W, A[, config])`
  * (actune/kernels/grouped_native.cu:90-115, grouped_big_m.cu:162-205) and the

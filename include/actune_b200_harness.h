@@ -32,17 +32,19 @@ int actune_harness_rope(void* qkv, const float* cos_t, const float* sin_t, int64
 int actune_harness_gated_act(const void* gu, void* out, int64_t T, int64_t I, int gelu, void* stream);
 
 /* actune_harness_rmsnorm (vector path: D % 256 == 0, D <= 8192, 16-byte aligned
- * buffers) that also quantizes the bf16 output it stores into the group-64 packed
- * activation format of actune_quantize_group64 (A bits): packed [T, D*A/8] u8 and
+ * buffers) that also quantizes the bf16 output it stores into the group-64
+ * activation format of actune_quantize_group64 (A bits): packed [T, D*A/8] u8, or
+ * with codes8 one int8 code per element [T, D] (actune_quantize_group64_codes), and
  * scales [T, D/64] f32, bit-identical to quantizing `out` with that entry. */
 int actune_harness_rmsnorm_q(const void* x, const void* residual, const void* weight, void* out, void* residual_out,
-                             int64_t T, int64_t D, float eps, int gemma, int A, uint8_t* packed, float* scales,
-                             void* stream);
+                             int64_t T, int64_t D, float eps, int gemma, int A, int codes8, uint8_t* packed,
+                             float* scales, void* stream);
 
 /* actune_harness_gated_act (I % 64 == 0, 16-byte aligned buffers) that also
- * quantizes its bf16 output: packed [T, I*A/8] u8, scales [T, I/64] f32. */
-int actune_harness_gated_act_q(const void* gu, void* out, int64_t T, int64_t I, int gelu, int A, uint8_t* packed,
-                               float* scales, void* stream);
+ * quantizes its bf16 output: packed [T, I*A/8] u8 (or int8 codes [T, I] with
+ * codes8), scales [T, I/64] f32. */
+int actune_harness_gated_act_q(const void* gu, void* out, int64_t T, int64_t I, int gelu, int A, int codes8,
+                               uint8_t* packed, float* scales, void* stream);
 
 #ifdef __cplusplus
 }

@@ -3,10 +3,12 @@ GEMM reads for calls of more than 32 token rows.
 
 * CPU: ``unpack_rows`` inverts the reference's little-endian packing (checked
   against the oracle's packer and unpacker for every width, ragged K included).
-* GPU: a layer with decoded codes gives bit-identical outputs to the packed path
-  for every sub-byte W x A pair, on both sides of the 32-row switch, with and
-  without bias; the bank runtime reports the bytes it added and the storage audit
-  of the packed versions is unchanged.
+* GPU: a layer with decoded codes (weights kept as int8 codes, activations
+  quantized to the same A-bit codes written one byte each, the W=8 / A=8 kernel)
+  gives bit-identical outputs to the packed path for every sub-byte W x A pair, on
+  both sides of the 32-row switch, with and without bias; the int8-code quantizer
+  writes exactly the unpacked packed codes; the bank runtime reports the bytes it
+  added and the storage audit of the packed versions is unchanged.
 """
 import numpy as np
 import pytest
@@ -46,9 +48,24 @@ def test_decoded_codes_bit_identical_to_packed(w, a, bias):
     assert added == 320 * 1024 and layer.decoded_weight.dtype == torch.uint8
     assert layer.decode_weight() == 0  # idempotent
     for m, x in xs.items():
-        weight, width = layer._weight_for(m)
-        assert (width == 8) == (m >= DECODED_MIN_TOKENS)
+        weight, width, a_kernel = layer.operands(m)
+        decoded = m >= DECODED_MIN_TOKENS
+        assert (width, a_kernel) == ((8, 8) if decoded else (w, a))
+        assert layer.activation_format(m) == (a, decoded and a < 8)
         assert torch.equal(layer(x), packed_out[m]), (w, a, m)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [2, 4, 8])
+def test_int8_code_quantizer_is_the_unpacked_packed_one(bits):
+    from actune_b200 import ops
+    from actune_b200.kernels.grouped import unpack_rows
+    torch.manual_seed(bits)
+    x = torch.randn(37, 1536, device="cuda", dtype=torch.bfloat16) * 3
+    packed, scales = ops.quantize_group64(x, bits)
+    codes, scales8 = ops.quantize_group64(x, bits, codes8=True)
+    assert codes.shape == (37, 1536) and torch.equal(scales8, scales)
+    assert torch.equal(codes.view(torch.int8), unpack_rows(packed, bits, 1536))
 
 
 @pytest.mark.gpu

@@ -303,32 +303,37 @@ def test_glue_kernels_quantize_like_the_quantizer(bits):
         r = torch.randn(9, d, device="cuda", dtype=torch.bfloat16) if with_res else None
         w = torch.randn(d, device="cuda", dtype=torch.bfloat16)
         ref_out, ref_res = H.rmsnorm(x, w, 1e-5, r, gemma)
-        out = torch.empty_like(x)
-        res_out = torch.empty_like(x) if with_res else None
-        packed = torch.empty(9, d * bits // 8, device="cuda", dtype=torch.uint8)
-        scales = torch.empty(9, d // 64, device="cuda", dtype=torch.float32)
-        rc = L.actune_harness_rmsnorm_q(H._p(x), H._p(r), H._p(w), H._p(out), H._p(res_out), 9, d,
-                                        ctypes.c_float(1e-5), int(gemma), bits, H._p(packed), H._p(scales), H._s(x))
-        assert rc == 0
-        torch.cuda.synchronize()
-        assert torch.equal(out, ref_out)
-        if with_res:
-            assert torch.equal(res_out, ref_res)
-        qp, qs = ops.quantize_group64(out, bits)
-        assert torch.equal(packed, qp) and torch.equal(scales, qs)
+        for codes8 in (0, 1):
+            width = 8 if codes8 else bits
+            out = torch.empty_like(x)
+            res_out = torch.empty_like(x) if with_res else None
+            packed = torch.empty(9, d * width // 8, device="cuda", dtype=torch.uint8)
+            scales = torch.empty(9, d // 64, device="cuda", dtype=torch.float32)
+            rc = L.actune_harness_rmsnorm_q(H._p(x), H._p(r), H._p(w), H._p(out), H._p(res_out), 9, d,
+                                            ctypes.c_float(1e-5), int(gemma), bits, codes8, H._p(packed),
+                                            H._p(scales), H._s(x))
+            assert rc == 0
+            torch.cuda.synchronize()
+            assert torch.equal(out, ref_out)
+            if with_res:
+                assert torch.equal(res_out, ref_res)
+            qp, qs = ops.quantize_group64(out, bits, codes8=bool(codes8))
+            assert torch.equal(packed, qp) and torch.equal(scales, qs)
     for inter, gelu in ((512, False), (11008, False), (1024, True)):
         gu = torch.randn(7, 2 * inter, device="cuda", dtype=torch.bfloat16)
         ref = H.gated_act(gu, gelu)
-        out = torch.empty_like(ref)
-        packed = torch.empty(7, inter * bits // 8, device="cuda", dtype=torch.uint8)
-        scales = torch.empty(7, inter // 64, device="cuda", dtype=torch.float32)
-        rc = L.actune_harness_gated_act_q(H._p(gu), H._p(out), 7, inter, int(gelu), bits, H._p(packed),
-                                          H._p(scales), H._s(gu))
-        assert rc == 0
-        torch.cuda.synchronize()
-        assert torch.equal(out, ref)
-        qp, qs = ops.quantize_group64(out, bits)
-        assert torch.equal(packed, qp) and torch.equal(scales, qs)
+        for codes8 in (0, 1):
+            width = 8 if codes8 else bits
+            out = torch.empty_like(ref)
+            packed = torch.empty(7, inter * width // 8, device="cuda", dtype=torch.uint8)
+            scales = torch.empty(7, inter // 64, device="cuda", dtype=torch.float32)
+            rc = L.actune_harness_gated_act_q(H._p(gu), H._p(out), 7, inter, int(gelu), bits, codes8, H._p(packed),
+                                              H._p(scales), H._s(gu))
+            assert rc == 0
+            torch.cuda.synchronize()
+            assert torch.equal(out, ref)
+            qp, qs = ops.quantize_group64(out, bits, codes8=bool(codes8))
+            assert torch.equal(packed, qp) and torch.equal(scales, qs)
 
 
 def test_small_oft_backbone_graph_vs_eager():
