@@ -380,6 +380,8 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
       CUtensorMap tw_b;
       rc = encode_map(&tw_b, w, N, K * W / 8, W == 8 ? 128 : 16 * W, bn_b, W == 8 ? Swz::B128 : Swz::None);
       if (rc != ACTUNE_OK) return rc;
+      // The first launch starts after the previous kernel completes (normal stream
+      // order), so the second, dependent on it, may read the same inputs at once.
       GemmParams pa = p, pb = p;
       pa.n_end = (int)(na * 128);
       pb.n_base = (int)(na * 128);
@@ -388,10 +390,13 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
       return cuda_status(e);
     }
   }
-  // The debug dots export always runs the one-CTA-per-SM form.
+  // The debug dots export always runs the one-CTA-per-SM form.  The one-CTA form is a
+  // dependent launch: it prefetches its first weight tiles while the previous kernel
+  // finishes.
   const bool x2 = is_x2_variant(variant) && dots == nullptr;
-  const cudaError_t e =
-      wt ? dispatch_wt_gemm(W, A, bn, ta, tw, p, stream) : dispatch_gemm(W, A, bn, x2, ta, tw, p, stream);
+  if (!wt && !x2) p.pdl_wait = 1;
+  const cudaError_t e = wt ? dispatch_wt_gemm(W, A, bn, ta, tw, p, stream)
+                           : dispatch_gemm(W, A, bn, x2, ta, tw, p, stream, !x2);
   return cuda_status(e);
 }
 
@@ -476,7 +481,8 @@ int run_rowwise(const uint8_t* a, int A, const float* a_scale, const uint8_t* w,
       return cuda_status(e);
     }
   }
-  return cuda_status(launch(bn, tw, p, false));
+  p.pdl_wait = 1;
+  return cuda_status(launch(bn, tw, p, true));
 }
 
 }  // namespace

@@ -188,6 +188,36 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 }
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Every kernel on the hot path is launched with programmatic stream serialization:
+// it may start while the kernel before it in the stream is still running (once all
+// of that kernel's CTAs have started and signalled), does what does not depend on
+// it (barrier set-up, tensor-memory allocation, descriptor prefetch, loads of the
+// resident weights), then waits in griddep_wait() before it reads anything the
+// previous kernel may have written or writes any global memory (an output buffer
+// may reuse memory the previous kernel still reads).  After a kernel that never
+// signals (a library kernel) the launch starts when that kernel completes.
+template <typename Kernel, typename... Args>
+cudaError_t launch_pdl(Kernel kernel, dim3 grid, int threads, int smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// Prologue of a dependent-launched kernel that reads its inputs from the start:
+// wait for the previous kernel, then let the next one start.
+__device__ __forceinline__ void griddep_enter() {
+  griddep_wait();
+  griddep_launch_dependents();
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -43,6 +43,7 @@ struct GemmParams {
   int rowwise_order;       // row-scaled modes: 0 (acc*as)*ws, 1 acc*(as*ws) (the per-row A4 native order)
   int gemv_boxes2d;        // decode: packed rows not whole 128-byte blocks, one 2-D box per block
   int a_box_rows;          // GEMM: token box height of the activation map (0: a whole 128-row tile)
+  int pdl_wait;            // dependent launch: wait for the previous kernel before reading its outputs
   int n_base, n_end;       // GEMM: output columns [n_base, n_end) of [0, N) (n_end 0: N)
 };
 
@@ -230,8 +231,9 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
   const int n_iters = (G + 1) >> 1;
   const int m0 = blockIdx.x * C::BM;
   const int n0 = p.n_base + blockIdx.y * BN;
-  // A launch that covers part of the columns lets the launch for the rest (made with
-  // programmatic stream serialization) start as soon as SMs come free.
+  // The next launch in the stream (made with programmatic stream serialization) may
+  // start as soon as SMs come free: the rest of a wave-tail split, which reads the
+  // same inputs, or a kernel that waits for this one before reading its output.
   if (threadIdx.x == 0) griddep_launch_dependents();
 
   if (threadIdx.x == 0) {
@@ -289,6 +291,11 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
         bar[j] = smem_u32(&full_raw[j]);
         xs[j] = j * x_step;
       }
+      // Dependent launch: the set-up above overlapped the previous kernel; the tiles
+      // are requested once it has completed.  (Requesting the first weight tiles
+      // before the wait measured slower: the extra path costs the ring loop more
+      // than the early loads save.)
+      if (p.pdl_wait) griddep_wait();
       uint32_t ph = 0;
       bool ok = true;
       for (int it0 = 0; it0 < n_iters && ok; it0 += S) {
@@ -422,6 +429,8 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
     // accumulation of the previous half, and the first half of the next stage
     // is loaded before the last half of this one is accumulated.  Activation
     // scales are fetched two stages ahead into static register slots.
+    // Activation scales and the output may belong to the previous kernel.
+    if (p.pdl_wait) griddep_wait();
     const int ew = warp - C::EPI_WARP0;
     const int q = warp & 3;      // TMEM lane quarter this warp may access
     const int e = ew >> 2;       // column slice

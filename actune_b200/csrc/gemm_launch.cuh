@@ -8,23 +8,6 @@
 
 namespace actune {
 
-// Launch with programmatic stream serialization (the dependent part of a
-// wave-tail split; see launch_group64_gemm in gemm_group64.cuh).
-template <typename Kernel, typename... Args>
-cudaError_t launch_pdl(Kernel kernel, dim3 grid, int threads, int smem, cudaStream_t stream, Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, args...);
-}
-
 template <int W, int A, int BN>
 cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm_wgt, const GemmParams& p,
                                 cudaStream_t stream, bool pdl) {

@@ -113,6 +113,8 @@ __global__ void __launch_bounds__(128) gemv_group64_kernel(const __grid_constant
     }
     fence_barrier_init();
   }
+  // Dependent launch: everything below reads the previous kernel's outputs.
+  griddep_enter();
   __syncthreads();
 
   // Producer: lanes 0 .. A_BLK-1 of warp 0 load the token boxes of a stage and the
@@ -364,6 +366,9 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI, WIDE>::THREADS, 1)
   const int n_blocks = (p.N + C::ROWS - 1) / C::ROWS;
   const int my_blocks = (int)blockIdx.x < n_blocks ? (n_blocks - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int total = my_blocks * n_stages;
+  // The next kernel (a dependent launch) may start as SMs come free; it waits for
+  // this one before reading what it writes.
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -397,28 +402,46 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI, WIDE>::THREADS, 1)
       const uint32_t mask = lanes == 32 ? 0xffffffffu : ((1u << lanes) - 1u);
       const uint32_t stage_tx = C::W_BYTES + (b2d ? C::A_BLK * C::TOK * 128 : Mb * C::A_BLK * 128) +
                                 ((DOTS || TW) ? 0 : Mb * C::GPS * 4);
+      // Dependent launch: the weight boxes of the first ring pass are requested before
+      // waiting for the previous kernel (they do not depend on it); tokens and scales after.
+      auto weight_box = [&](int it) {
+        const int s = it % C::STAGES;
+        const int rb = (int)blockIdx.x + (it / n_stages) * (int)gridDim.x, st = it % n_stages;
+        uint8_t* base = smem + s * C::STAGE_BYTES;
+        if (b2d) tma_load_2d(base + blk * (C::ROWS * 128), &tm_wgt, (st * C::W_BLK + blk) * 128, rb * C::ROWS, &full_bar[s]);
+        else tma_load_3d(base, &tm_wgt, 0, rb * C::ROWS, st * C::W_BLK, &full_bar[s]);
+      };
+      const int pre = p.pdl_wait ? min(C::STAGES, total) : 0;
+      if (pre > 0) {
+        if (lane == 0)
+          for (int it = 0; it < pre; ++it) mbar_arrive_expect_tx(&full_bar[it], stage_tx);
+        __syncwarp(mask);
+        if (kind == 0)
+          for (int it = 0; it < pre; ++it) weight_box(it);
+        griddep_wait();
+      }
       int issued = 0;
       for (int it = 0; it < total; ++it) {
         const int s = it % C::STAGES;
+        const bool prefetched = it < pre;
         bool ok = true;
-        if (lane == 0) {
+        if (lane == 0 && !prefetched) {
           if (it >= C::STAGES) ok = mbar_wait(&empty_bar[s], ((it / C::STAGES) & 1) ^ 1, kGv4SiteEmpty);
           if (ok) mbar_arrive_expect_tx(&full_bar[s], stage_tx);
         }
         if (!__shfl_sync(mask, ok, 0)) break;
-        const int rb = (int)blockIdx.x + (it / n_stages) * (int)gridDim.x, st = it % n_stages;
+        const int st = it % n_stages;
         uint8_t* base = smem + s * C::STAGE_BYTES;
-        if (b2d) {
-          if (kind == 0)
-            tma_load_2d(base + blk * (C::ROWS * 128), &tm_wgt, (st * C::W_BLK + blk) * 128, rb * C::ROWS, &full_bar[s]);
-          else if (kind == 1)
+        if (kind == 0) {
+          if (!prefetched) weight_box(it);
+        } else if (b2d) {
+          if (kind == 1)
             tma_load_2d(base + C::W_BYTES + blk * (C::TOK * 128), &tm_act, (st * C::A_BLK + blk) * 128, 0,
                         &full_bar[s]);
           else if (!DOTS && !TW)
             tma_load_2d(base + C::W_BYTES + C::A_BYTES, &tm_scale, st * C::GPS, 0, &full_bar[s]);
         } else {
-          if (lane == 0) tma_load_3d(base, &tm_wgt, 0, rb * C::ROWS, st * C::W_BLK, &full_bar[s]);
-          else if (lane == 1) tma_load_3d(base + C::W_BYTES, &tm_act, 0, 0, st * C::A_BLK, &full_bar[s]);
+          if (lane == 1) tma_load_3d(base + C::W_BYTES, &tm_act, 0, 0, st * C::A_BLK, &full_bar[s]);
           else if (!DOTS && !TW) tma_load_2d(base + C::W_BYTES + C::A_BYTES, &tm_scale, st * C::GPS, 0, &full_bar[s]);
         }
         ++issued;
@@ -431,6 +454,7 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI, WIDE>::THREADS, 1)
     }
   } else if (warp < C::DOT_WARPS) {
     // ------------------------------------------------------------ dots
+    if (DOTS && p.pdl_wait) griddep_wait();  // the dots export writes global memory
     const int r = warp & 1, q = warp >> 1;  // 16-row group, K-lane
     const int gid = lane >> 2, t = lane & 3;
     uint32_t ow0[C::GPQ], ow1[C::GPQ], oa_lo[C::GPQ], oa_hi[C::GPQ];
@@ -507,6 +531,7 @@ __global__ void __launch_bounds__(Gemv4Cfg<W, A, HI, WIDE>::THREADS, 1)
     }
   } else if constexpr (!DOTS) {
     // ------------------------------------------------------------ chain
+    if (p.pdl_wait) griddep_wait();  // activation scales and the output may belong to the previous kernel
     const int blk8 = warp - C::DOT_WARPS, r = blk8 >> 1;  // 8-row block, its 16-row group
     const int gid = lane >> 2, t = lane & 3;
     const bool tok0 = gid < Mb, tok1 = HI && gid + 8 < Mb;
@@ -624,8 +649,9 @@ static cudaError_t launch_gemv4_hi(const CUtensorMap& ta, const CUtensorMap& tw,
   if (e != cudaSuccess) return e;
   const int blocks = (p.N + C::ROWS - 1) / C::ROWS;
   const int grid = blocks < num_sms ? blocks : num_sms;
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, ts, p);
-  return cudaGetLastError();
+  GemmParams pp = p;
+  pp.pdl_wait = 1;
+  return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM_BYTES, stream, ta, tw, ts, pp);
 }
 
 template <int W, int A>
@@ -656,8 +682,7 @@ static cudaError_t launch_gemv_t(const CUtensorMap& ta, const CUtensorMap& tw, c
   const cudaError_t e = dots ? ensure_smem_limit<k_dots>(C::SMEM_BYTES) : ensure_smem_limit<k_out>(C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   auto kernel = dots ? k_dots : k_out;
-  kernel<<<(p.N + C::ROWS - 1) / C::ROWS, C::THREADS, C::SMEM_BYTES, stream>>>(ta, tw, p);
-  return cudaGetLastError();
+  return launch_pdl(kernel, dim3((p.N + C::ROWS - 1) / C::ROWS), C::THREADS, C::SMEM_BYTES, stream, ta, tw, p);
 }
 
 cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap* ts,

@@ -26,6 +26,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
                                                       __nv_bfloat16* __restrict__ out,
                                                       __nv_bfloat16* __restrict__ residual_out, int D, float eps,
                                                       int gemma) {
+  actune::griddep_enter();  // dependent launch: the inputs are the previous kernel's outputs
   extern __shared__ float row[];
   __shared__ float red[8];
   const int64_t t = blockIdx.x;
@@ -68,6 +69,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
 // heads of a fused [T, (Hq + 2*Hkv) * Dh] buffer.  cos/sin: [T, Dh/2] fp32.
 __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ cos_t,
                             const float* __restrict__ sin_t, int T, int Hq, int Hkv, int Dh) {
+  actune::griddep_enter();  // dependent launch: the inputs are the previous kernel's outputs
   const int half = Dh / 2;
   const int heads = Hq + Hkv;  // q and k heads (v untouched)
   const int64_t total = (int64_t)T * heads * half;
@@ -88,6 +90,7 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __rest
 // act = SiLU (Llama) or tanh-GELU (Gemma).
 __global__ void gated_act_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out, int T,
                                  int I, int gelu) {
+  actune::griddep_enter();  // dependent launch: the inputs are the previous kernel's outputs
   const int64_t total = (int64_t)T * I;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t t = i / I, c = i % I;
@@ -135,6 +138,7 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const __nv_bfloat16* _
                                                           __nv_bfloat16* __restrict__ residual_out, int D, float eps,
                                                           int gemma, uint8_t* __restrict__ qpacked,
                                                           float* __restrict__ qscales) {
+  actune::griddep_enter();  // dependent launch: the inputs are the previous kernel's outputs
   __shared__ float red[8];
   const int64_t base = (int64_t)blockIdx.x * D;
   float v[CPT][8];
@@ -193,6 +197,7 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const __nv_bfloat16* _
 // of one head (half % 8 == 0).
 __global__ void __launch_bounds__(256) rope_vec_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ cos_t,
                                                        const float* __restrict__ sin_t, int Hq, int Hkv, int Dh) {
+  actune::griddep_enter();  // dependent launch: the inputs are the previous kernel's outputs
   const int half = Dh / 2, per_head = half / 8, heads = Hq + Hkv;
   const int t = blockIdx.x;
   __nv_bfloat16* row = qkv + (int64_t)t * (Hq + 2 * Hkv) * Dh;
@@ -228,6 +233,7 @@ __global__ void __launch_bounds__(256) gated_act_vec_kernel(const __nv_bfloat16*
                                                             __nv_bfloat16* __restrict__ out, int T, int I, int gelu,
                                                             uint8_t* __restrict__ qpacked,
                                                             float* __restrict__ qscales) {
+  actune::griddep_enter();  // dependent launch: the inputs are the previous kernel's outputs
   const int per_row = I / 8;
   const int64_t total = (int64_t)T * per_row;
   const int lane = threadIdx.x & 31;
@@ -282,11 +288,11 @@ cudaError_t launch_rmsnorm_q(const __nv_bfloat16* xb, const __nv_bfloat16* rb, c
                              __nv_bfloat16* ob, __nv_bfloat16* rob, int64_t T, int64_t D, float eps, int gemma,
                              uint8_t* qp, float* qs, cudaStream_t cs) {
   if (D <= 2048)
-    rmsnorm_vec_kernel<1, QA, QOUT><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
+    (void)actune::launch_pdl(rmsnorm_vec_kernel<1, QA, QOUT>, dim3((unsigned)T), 256, 0, cs, xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
   else if (D <= 4096)
-    rmsnorm_vec_kernel<2, QA, QOUT><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
+    (void)actune::launch_pdl(rmsnorm_vec_kernel<2, QA, QOUT>, dim3((unsigned)T), 256, 0, cs, xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
   else
-    rmsnorm_vec_kernel<4, QA, QOUT><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
+    (void)actune::launch_pdl(rmsnorm_vec_kernel<4, QA, QOUT>, dim3((unsigned)T), 256, 0, cs, xb, rb, wb, ob, rob, (int)D, eps, gemma, qp, qs);
   return cudaGetLastError();
 }
 
@@ -309,12 +315,12 @@ int actune_harness_rmsnorm(const void* x, const void* residual, const void* weig
     const auto* wb = reinterpret_cast<const __nv_bfloat16*>(weight);
     auto* ob = reinterpret_cast<__nv_bfloat16*>(out);
     auto* rob = reinterpret_cast<__nv_bfloat16*>(residual_out);
-    if (D <= 2048) rmsnorm_vec_kernel<1, 0><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, nullptr, nullptr);
-    else if (D <= 4096) rmsnorm_vec_kernel<2, 0><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, nullptr, nullptr);
-    else rmsnorm_vec_kernel<4, 0><<<(unsigned)T, 256, 0, cs>>>(xb, rb, wb, ob, rob, (int)D, eps, gemma, nullptr, nullptr);
+    if (D <= 2048) (void)actune::launch_pdl(rmsnorm_vec_kernel<1, 0>, dim3((unsigned)T), 256, 0, cs, xb, rb, wb, ob, rob, (int)D, eps, gemma, nullptr, nullptr);
+    else if (D <= 4096) (void)actune::launch_pdl(rmsnorm_vec_kernel<2, 0>, dim3((unsigned)T), 256, 0, cs, xb, rb, wb, ob, rob, (int)D, eps, gemma, nullptr, nullptr);
+    else (void)actune::launch_pdl(rmsnorm_vec_kernel<4, 0>, dim3((unsigned)T), 256, 0, cs, xb, rb, wb, ob, rob, (int)D, eps, gemma, nullptr, nullptr);
     return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
   }
-  rmsnorm_kernel<<<(unsigned)T, 256, D * sizeof(float), reinterpret_cast<cudaStream_t>(stream)>>>(
+  (void)actune::launch_pdl(rmsnorm_kernel, dim3((unsigned)T), 256, D * sizeof(float), reinterpret_cast<cudaStream_t>(stream), 
       reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(residual),
       reinterpret_cast<const __nv_bfloat16*>(weight), reinterpret_cast<__nv_bfloat16*>(out),
       reinterpret_cast<__nv_bfloat16*>(residual_out), (int)D, eps, gemma);
@@ -327,12 +333,12 @@ int actune_harness_rope(void* qkv, const float* cos_t, const float* sin_t, int64
     return ACTUNE_ERR_INVALID_VALUE;
   if (T == 0) return ACTUNE_OK;
   if ((Dh / 2) % 8 == 0 && aligned16(qkv) && aligned16(cos_t) && aligned16(sin_t)) {
-    rope_vec_kernel<<<(unsigned)T, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+    (void)actune::launch_pdl(rope_vec_kernel, dim3((unsigned)T), 256, 0, reinterpret_cast<cudaStream_t>(stream), 
         reinterpret_cast<__nv_bfloat16*>(qkv), cos_t, sin_t, Hq, Hkv, Dh);
     return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
   }
   const int64_t n = T * (Hq + Hkv) * (Dh / 2);
-  rope_kernel<<<grid_for(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  (void)actune::launch_pdl(rope_kernel, dim3(grid_for(n)), 256, 0, reinterpret_cast<cudaStream_t>(stream), 
       reinterpret_cast<__nv_bfloat16*>(qkv), cos_t, sin_t, (int)T, Hq, Hkv, Dh);
   return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
 }
@@ -341,12 +347,12 @@ int actune_harness_gated_act(const void* gu, void* out, int64_t T, int64_t I, in
   if (T < 0 || I <= 0 || gu == nullptr || out == nullptr) return ACTUNE_ERR_INVALID_VALUE;
   if (T == 0) return ACTUNE_OK;
   if (I % 8 == 0 && aligned16(gu) && aligned16(out)) {
-    gated_act_vec_kernel<0><<<grid_for(T * I / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+    (void)actune::launch_pdl(gated_act_vec_kernel<0>, dim3(grid_for(T * I / 8)), 256, 0, reinterpret_cast<cudaStream_t>(stream), 
         reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(out), (int)T, (int)I, gelu,
         nullptr, nullptr);
     return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
   }
-  gated_act_kernel<<<grid_for(T * I), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  (void)actune::launch_pdl(gated_act_kernel, dim3(grid_for(T * I)), 256, 0, reinterpret_cast<cudaStream_t>(stream), 
       reinterpret_cast<const __nv_bfloat16*>(gu), reinterpret_cast<__nv_bfloat16*>(out), (int)T, (int)I, gelu);
   return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
 }
@@ -387,11 +393,11 @@ int actune_harness_gated_act_q(const void* gu, void* out, int64_t T, int64_t I, 
   auto* o = reinterpret_cast<__nv_bfloat16*>(out);
   auto* cs = reinterpret_cast<cudaStream_t>(stream);
   const int grid = grid_for(T * I / 8);
-  if (A == 8) gated_act_vec_kernel<8><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
-  else if (A == 4 && codes8) gated_act_vec_kernel<4, 8><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
-  else if (A == 4) gated_act_vec_kernel<4><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
-  else if (codes8) gated_act_vec_kernel<2, 8><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
-  else gated_act_vec_kernel<2><<<grid, 256, 0, cs>>>(g, o, (int)T, (int)I, gelu, packed, scales);
+  if (A == 8) (void)actune::launch_pdl(gated_act_vec_kernel<8>, dim3(grid), 256, 0, cs, g, o, (int)T, (int)I, gelu, packed, scales);
+  else if (A == 4 && codes8) (void)actune::launch_pdl(gated_act_vec_kernel<4, 8>, dim3(grid), 256, 0, cs, g, o, (int)T, (int)I, gelu, packed, scales);
+  else if (A == 4) (void)actune::launch_pdl(gated_act_vec_kernel<4>, dim3(grid), 256, 0, cs, g, o, (int)T, (int)I, gelu, packed, scales);
+  else if (codes8) (void)actune::launch_pdl(gated_act_vec_kernel<2, 8>, dim3(grid), 256, 0, cs, g, o, (int)T, (int)I, gelu, packed, scales);
+  else (void)actune::launch_pdl(gated_act_vec_kernel<2>, dim3(grid), 256, 0, cs, g, o, (int)T, (int)I, gelu, packed, scales);
   return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
 }
 

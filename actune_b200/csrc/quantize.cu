@@ -60,6 +60,7 @@ __device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
 template <int A, typename T, int OUT = A>
 __global__ void __launch_bounds__(256) quantize_group64_kernel(const T* __restrict__ x, uint8_t* __restrict__ packed,
                                                                float* __restrict__ scales, int64_t groups) {
+  griddep_enter();  // dependent launch: x is the previous kernel's output
   const int lane = threadIdx.x & 31;
   const int seg = lane >> 3, l8 = lane & 7;
   const int64_t warp_global = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -211,15 +212,15 @@ static cudaError_t launch_quantize_t(const T* x, int64_t groups, int A, bool cod
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   if (codes8 && A == 2)
-    quantize_group64_kernel<2, T, 8><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups);
+    (void)launch_pdl(quantize_group64_kernel<2, T, 8>, dim3((unsigned)blocks), threads, 0, stream, x, packed, scales, groups);
   else if (codes8 && A == 4)
-    quantize_group64_kernel<4, T, 8><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups);
+    (void)launch_pdl(quantize_group64_kernel<4, T, 8>, dim3((unsigned)blocks), threads, 0, stream, x, packed, scales, groups);
   else if (A == 2)
-    quantize_group64_kernel<2, T><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups);
+    (void)launch_pdl(quantize_group64_kernel<2, T>, dim3((unsigned)blocks), threads, 0, stream, x, packed, scales, groups);
   else if (A == 4)
-    quantize_group64_kernel<4, T><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups);
+    (void)launch_pdl(quantize_group64_kernel<4, T>, dim3((unsigned)blocks), threads, 0, stream, x, packed, scales, groups);
   else
-    quantize_group64_kernel<8, T><<<(unsigned)blocks, threads, 0, stream>>>(x, packed, scales, groups);
+    (void)launch_pdl(quantize_group64_kernel<8, T>, dim3((unsigned)blocks), threads, 0, stream, x, packed, scales, groups);
   return cudaGetLastError();
 }
 
@@ -254,6 +255,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
   constexpr float kPos = float((1 << (BITS - 1)) - 1);
   constexpr float kNeg = -float(1 << (BITS - 1));
   __shared__ float red[8];
+  griddep_enter();  // dependent launch: x is the previous kernel's output
   const int64_t row = blockIdx.x;
   const T* xr = x + row * K;
   constexpr int C = CPT > 0 ? CPT : 1;
@@ -319,10 +321,10 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
 template <typename T, int BITS>
 static cudaError_t launch_rows_t(const T* x, int64_t M, int64_t K, uint8_t* codes, float* scales, cudaStream_t s) {
   const unsigned grid = (unsigned)M;
-  if (K <= 2048) quantize_rows_kernel<T, 1, BITS><<<grid, 256, 0, s>>>(x, codes, scales, K);
-  else if (K <= 4096) quantize_rows_kernel<T, 2, BITS><<<grid, 256, 0, s>>>(x, codes, scales, K);
-  else if (K <= 8192) quantize_rows_kernel<T, 4, BITS><<<grid, 256, 0, s>>>(x, codes, scales, K);
-  else quantize_rows_kernel<T, 0, BITS><<<grid, 256, 0, s>>>(x, codes, scales, K);
+  if (K <= 2048) (void)launch_pdl(quantize_rows_kernel<T, 1, BITS>, dim3(grid), 256, 0, s, x, codes, scales, K);
+  else if (K <= 4096) (void)launch_pdl(quantize_rows_kernel<T, 2, BITS>, dim3(grid), 256, 0, s, x, codes, scales, K);
+  else if (K <= 8192) (void)launch_pdl(quantize_rows_kernel<T, 4, BITS>, dim3(grid), 256, 0, s, x, codes, scales, K);
+  else (void)launch_pdl(quantize_rows_kernel<T, 0, BITS>, dim3(grid), 256, 0, s, x, codes, scales, K);
   return cudaGetLastError();
 }
 
