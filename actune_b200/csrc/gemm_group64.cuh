@@ -24,6 +24,8 @@
 //               accumulators, final scale/bias/convert/store
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace actune {
@@ -71,6 +73,11 @@ struct Group64Cfg {
   static constexpr int CVT_WARPS = CONVERT ? (OCC == 1 ? 4 : 2) : 0;
   static constexpr int EPI_WARP0 = 2 + CVT_WARPS;
   static constexpr int THREADS = 32 * EPI_WARP0 + 128 * EPI_WG;
+  // The tile kernel adds a second MMA-issuing warp after the epilogue warps: the two
+  // issue alternate stages, so that one thread's barrier waits and commits overlap
+  // the other's MMAs (one issuing thread is held for each MMA's duration).
+  static constexpr int MMA2_WARP = THREADS / 32;
+  static constexpr int TILE_THREADS = THREADS + 32;
   // Per-stage shared-memory layout: [act int8 | wgt int8 | act packed | wgt packed].
   static constexpr int OP_A_BYTES = BM * KS;        // 16 KB, SW128 K-major
   static constexpr int OP_W_BYTES = BN * KS;
@@ -212,7 +219,7 @@ __device__ __forceinline__ void store_dots(const GemmParams& p, int m, int col, 
 // 64-group; the epilogue reads it once, converts it exactly (round to nearest) and
 // applies the per-token scale (p.act_scale[m]), then ws / bias as below.
 template <int W, int A, int BN, bool DOTS, bool TW = false, int OCC = 1>
-__global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
+__global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::TILE_THREADS, OCC)
     group64_gemm_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
                         const GemmParams p) {
   using C = Group64Cfg<W, A, BN, OCC>;
@@ -222,7 +229,7 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
   __shared__ __align__(8) uint64_t acc_full[C::NPAIR];
   __shared__ __align__(8) uint64_t acc_empty[C::NPAIR];
-  __shared__ __align__(8) uint64_t mma_done;
+  __shared__ __align__(8) uint64_t mma_done[2];
   __shared__ uint32_t tmem_holder;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -246,7 +253,8 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4 * C::EPI_WG);
     }
-    mbar_init(&mma_done, 1);
+    mbar_init(&mma_done[0], 1);
+    mbar_init(&mma_done[1], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -321,26 +329,31 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
       for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it)
         mbar_wait(&full_raw[it % C::STAGES], (it / C::STAGES) & 1, kSiteDrain);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    // Per stage: wait operands, wait the accumulator pair, 4 MMAs, 2 commits.
-    // An MMA reads its register operands when the tensor core takes it, so the
-    // descriptors live in two register sets used by alternate stages and each set
-    // is rewritten only after the other stage's MMAs have been issued.
-    if (lane == 0) {
-      constexpr int S = C::STAGES;
-      constexpr uint32_t idesc = idesc_i8(C::BM, BN);
-      const uint64_t desc_a0 = smem_desc_sw128(smem_u32(smem));
-      const uint64_t desc_w0 = smem_desc_sw128(smem_u32(smem) + C::OP_A_BYTES);
-      constexpr uint64_t kStageStep = (uint64_t)(C::STAGE_BYTES >> 4);
-      uint64_t da[2][4], dw[2][4];
-#pragma unroll
-      for (int q = 0; q < 2; ++q)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          da[q][k] = desc_a0 + kStageStep * q + 2 * k;
-          dw[q][k] = desc_w0 + kStageStep * q + 2 * k;
-        }
+  } else if (warp == 1 || warp == C::MMA2_WARP) {
+    // ------------------------------------------------------------ MMA issuers
+    // Warp 1 issues the even stages, the last warp the odd ones (warp 1 all of them in
+    // the row-scaled mode, whose stages accumulate into one buffer, and with a single
+    // accumulator pair): one issuing
+    // thread is held for each MMA's duration, so one issuer's barrier waits and
+    // commits overlap the other's MMAs.  With an even ring depth and an even number
+    // of accumulator pairs, a ring slot and an accumulator pair always belong to the
+    // same issuer, whose commits track its own MMAs.
+    // Per stage: wait operands, wait the accumulator pair, 4 MMAs, 2 commits.  An MMA
+    // reads its register operands when the tensor core takes it: each issuer keeps
+    // the descriptors of its own ring slots in registers of their own (never
+    // rewritten); the single row-scaled issuer alternates two sets, each rewritten
+    // only after the other stage's MMAs have been issued.
+    // Two issuers need an even number of accumulator pairs (else one issuer).
+    constexpr bool TWO = !TW && C::NPAIR % 2 == 0;
+    static_assert(C::STAGES % 2 == 0, "even ring depth");
+    constexpr int S = C::STAGES;
+    constexpr uint32_t idesc = idesc_i8(C::BM, BN);
+    const uint64_t desc_a0 = smem_desc_sw128(smem_u32(smem));
+    const uint64_t desc_w0 = smem_desc_sw128(smem_u32(smem) + C::OP_A_BYTES);
+    constexpr uint64_t kStageStep = (uint64_t)(C::STAGE_BYTES >> 4);
+    const int who = warp == 1 ? 0 : 1;
+    auto issue = [&](auto parity_tag) {
+      constexpr int PAR = decltype(parity_tag)::value;
       uint32_t dacc[C::NPAIR][2], bacc[C::NPAIR], bempty[S];
 #pragma unroll
       for (int pr = 0; pr < C::NPAIR; ++pr) {
@@ -352,27 +365,42 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
       for (int j = 0; j < S; ++j) bempty[j] = smem_u32(&empty_bar[j]);
       uint32_t ph = 0;
       bool ok = true;
-      for (int it0 = 0; it0 < n_iters && ok; it0 += S) {
+      if constexpr (!TWO) {
+        uint64_t da[2][4], dw[2][4];
 #pragma unroll
-        for (int j = 0; j < S; ++j) {
-          const int it = it0 + j;
-          if (it >= n_iters) break;
-          const int pr = j % C::NPAIR;
-          const int q = j & 1;
-          uint64_t* ready = C::CONVERT ? &full_op[j] : &full_raw[j];
-          if (!mbar_wait(ready, ph, kSiteMmaFull) ||
-              (!TW && !mbar_wait(&acc_empty[pr], ((it / C::NPAIR) & 1) ^ 1, kSiteMmaAcc))) {
-            ok = false;
-            break;
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            da[q][k] = desc_a0 + kStageStep * q + 2 * k;
+            dw[q][k] = desc_w0 + kStageStep * q + 2 * k;
           }
-          tc_fence_after();
-          if constexpr (TW) {
-            // Every K slice of every stage into one accumulator.
-            mma_i8(dacc[0][0], da[q][0], dw[q][0], idesc, it > 0 ? 1u : 0u);
-            mma_i8(dacc[0][0], da[q][1], dw[q][1], idesc, 1u);
-            mma_i8(dacc[0][0], da[q][2], dw[q][2], idesc, 1u);
-            mma_i8(dacc[0][0], da[q][3], dw[q][3], idesc, 1u);
-            if (it == n_iters - 1) mma_commit_u32(bacc[0]);
+        for (int it0 = 0; it0 < n_iters && ok; it0 += S) {
+#pragma unroll
+          for (int j = 0; j < S; ++j) {
+            const int it = it0 + j;
+            if (it >= n_iters) break;
+            const int q = j & 1, pr = j % C::NPAIR;
+            uint64_t* ready = C::CONVERT ? &full_op[j] : &full_raw[j];
+            if (!mbar_wait(ready, ph, kSiteMmaFull) ||
+                (!TW && !mbar_wait(&acc_empty[pr], ((it / C::NPAIR) & 1) ^ 1, kSiteMmaAcc))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            if constexpr (TW) {
+              // Every K slice of every stage into one accumulator.
+              mma_i8(dacc[0][0], da[q][0], dw[q][0], idesc, it > 0 ? 1u : 0u);
+              mma_i8(dacc[0][0], da[q][1], dw[q][1], idesc, 1u);
+              mma_i8(dacc[0][0], da[q][2], dw[q][2], idesc, 1u);
+              mma_i8(dacc[0][0], da[q][3], dw[q][3], idesc, 1u);
+              if (it == n_iters - 1) mma_commit_u32(bacc[0]);
+            } else {
+              mma_i8(dacc[pr][0], da[q][0], dw[q][0], idesc, 0u);
+              mma_i8(dacc[pr][0], da[q][1], dw[q][1], idesc, 1u);
+              mma_i8(dacc[pr][1], da[q][2], dw[q][2], idesc, 0u);
+              mma_i8(dacc[pr][1], da[q][3], dw[q][3], idesc, 1u);
+              mma_commit_u32(bacc[pr]);
+            }
             mma_commit_u32(bempty[j]);
             const int jn = (j + 1) % S;
 #pragma unroll
@@ -380,29 +408,50 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::THREADS, OCC)
               da[q ^ 1][k] = desc_a0 + kStageStep * jn + 2 * k;
               dw[q ^ 1][k] = desc_w0 + kStageStep * jn + 2 * k;
             }
-            continue;
           }
-          // Always both groups: past the end of K (odd G) the tiles are the
-          // TMA's zero fill, the dots are 0 and the epilogue gives them scale 0.
-          mma_i8(dacc[pr][0], da[q][0], dw[q][0], idesc, 0u);  // group 2it:   K bytes 0..31
-          mma_i8(dacc[pr][0], da[q][1], dw[q][1], idesc, 1u);  //              K bytes 32..63
-          mma_i8(dacc[pr][1], da[q][2], dw[q][2], idesc, 0u);  // group 2it+1: K bytes 64..95
-          mma_i8(dacc[pr][1], da[q][3], dw[q][3], idesc, 1u);  //              K bytes 96..127
-          mma_commit_u32(bacc[pr]);
-          mma_commit_u32(bempty[j]);
-          // The other register set was read by the previous stage's MMAs, issued a
-          // whole stage ago; it now takes the next ring slot's descriptors.
-          const int jn = (j + 1) % S;
+          ph ^= 1;
+        }
+      } else {
+        constexpr int NS = S / 2;  // ring slots PAR, PAR + 2, ...
+        uint64_t da[NS][4], dw[NS][4];
+#pragma unroll
+        for (int u = 0; u < NS; ++u)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            da[q ^ 1][k] = desc_a0 + kStageStep * jn + 2 * k;
-            dw[q ^ 1][k] = desc_w0 + kStageStep * jn + 2 * k;
+            da[u][k] = desc_a0 + kStageStep * (PAR + 2 * u) + 2 * k;
+            dw[u][k] = desc_w0 + kStageStep * (PAR + 2 * u) + 2 * k;
           }
+        for (int it0 = 0; it0 < n_iters && ok; it0 += S) {
+#pragma unroll
+          for (int j = PAR; j < S; j += 2) {
+            const int it = it0 + j;
+            if (it >= n_iters) break;
+            const int pr = j % C::NPAIR, u = j / 2;
+            uint64_t* ready = C::CONVERT ? &full_op[j] : &full_raw[j];
+            if (!mbar_wait(ready, ph, kSiteMmaFull) ||
+                !mbar_wait(&acc_empty[pr], ((it / C::NPAIR) & 1) ^ 1, kSiteMmaAcc)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            // Always both groups: past the end of K (odd G) the tiles are the
+            // TMA's zero fill, the dots are 0 and the epilogue gives them scale 0.
+            mma_i8(dacc[pr][0], da[u][0], dw[u][0], idesc, 0u);  // group 2it:   K bytes 0..31
+            mma_i8(dacc[pr][0], da[u][1], dw[u][1], idesc, 1u);  //              K bytes 32..63
+            mma_i8(dacc[pr][1], da[u][2], dw[u][2], idesc, 0u);  // group 2it+1: K bytes 64..95
+            mma_i8(dacc[pr][1], da[u][3], dw[u][3], idesc, 1u);  //              K bytes 96..127
+            mma_commit_u32(bacc[pr]);
+            mma_commit_u32(bempty[j]);
+          }
+          ph ^= 1;
         }
-        ph ^= 1;
       }
-      mma_commit(&mma_done);
-      mbar_wait(&mma_done, 0, kSiteMmaDone);
+    };
+    if (lane == 0) {
+      if (who == 0) issue(std::integral_constant<int, 0>{});
+      else if constexpr (TWO) issue(std::integral_constant<int, 1>{});
+      mma_commit(&mma_done[who]);
+      mbar_wait(&mma_done[who], 0, kSiteMmaDone);
     }
   } else if (warp < C::EPI_WARP0) {
     // ------------------------------------------------------------ converters

@@ -20,8 +20,8 @@ cudaError_t launch_group64_gemm(const CUtensorMap& tm_act, const CUtensorMap& tm
   auto kernel = dots ? k_dots : k_out;
   const int n_end = p.n_end > 0 ? p.n_end : p.N;
   const dim3 grid((p.M + C::BM - 1) / C::BM, (n_end - p.n_base + BN - 1) / BN);
-  if (pdl) return launch_pdl(kernel, grid, C::THREADS, C::SMEM_BYTES, stream, tm_act, tm_wgt, p);
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
+  if (pdl) return launch_pdl(kernel, grid, C::TILE_THREADS, C::SMEM_BYTES, stream, tm_act, tm_wgt, p);
+  kernel<<<grid, C::TILE_THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
   return cudaGetLastError();
 }
 
@@ -35,7 +35,7 @@ cudaError_t launch_group64_gemm_x2(const CUtensorMap& tm_act, const CUtensorMap&
   const cudaError_t e = ensure_smem_limit<kernel>(C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   const dim3 grid((p.M + C::BM - 1) / C::BM, (p.N + BN - 1) / BN);
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
+  kernel<<<grid, C::TILE_THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
   return cudaGetLastError();
 }
 
@@ -48,8 +48,8 @@ cudaError_t launch_group64_tokenwise(const CUtensorMap& tm_act, const CUtensorMa
   if (e != cudaSuccess) return e;
   const int n_end = p.n_end > 0 ? p.n_end : p.N;
   const dim3 grid((p.M + C::BM - 1) / C::BM, (n_end - p.n_base + BN - 1) / BN);
-  if (pdl) return launch_pdl(kernel, grid, C::THREADS, C::SMEM_BYTES, stream, tm_act, tm_wgt, p);
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
+  if (pdl) return launch_pdl(kernel, grid, C::TILE_THREADS, C::SMEM_BYTES, stream, tm_act, tm_wgt, p);
+  kernel<<<grid, C::TILE_THREADS, C::SMEM_BYTES, stream>>>(tm_act, tm_wgt, p);
   return cudaGetLastError();
 }
 
