@@ -195,8 +195,11 @@ __global__ void __launch_bounds__(256) rmsnorm_vec_kernel(const __nv_bfloat16* _
 
 // Rotary embedding, one CTA per token; thread handles 8 consecutive rotation pairs
 // of one head (half % 8 == 0).
+// With `cache` (one key/value head): the token's rotated key and its value are also
+// written to cache[b, offset + t, 0 / 1, :] for row b * seq + t.
 __global__ void __launch_bounds__(256) rope_vec_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ cos_t,
-                                                       const float* __restrict__ sin_t, int Hq, int Hkv, int Dh) {
+                                                       const float* __restrict__ sin_t, int Hq, int Hkv, int Dh,
+                                                       __nv_bfloat16* __restrict__ cache, int seq, int Tc, int offset) {
   actune::griddep_enter();  // dependent launch: the inputs are the previous kernel's outputs
   const int half = Dh / 2, per_head = half / 8, heads = Hq + Hkv;
   const int t = blockIdx.x;
@@ -221,6 +224,13 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(__nv_bfloat16* __restrict
     }
     *reinterpret_cast<uint4*>(b + j) = pack8(o1);
     *reinterpret_cast<uint4*>(b + j + half) = pack8(o2);
+  }
+  if (cache != nullptr) {
+    __syncthreads();  // the rotated key is complete
+    const __nv_bfloat16* kv = row + Hq * Dh;  // key then value, Dh each
+    __nv_bfloat16* dst = cache + ((int64_t)(t / seq) * Tc + offset + t % seq) * 2 * Dh;
+    for (int c = threadIdx.x; c < 2 * Dh / 8; c += blockDim.x)
+      reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(kv)[c];
   }
 }
 
@@ -333,13 +343,26 @@ int actune_harness_rope(void* qkv, const float* cos_t, const float* sin_t, int64
     return ACTUNE_ERR_INVALID_VALUE;
   if (T == 0) return ACTUNE_OK;
   if ((Dh / 2) % 8 == 0 && aligned16(qkv) && aligned16(cos_t) && aligned16(sin_t)) {
-    (void)actune::launch_pdl(rope_vec_kernel, dim3((unsigned)T), 256, 0, reinterpret_cast<cudaStream_t>(stream), 
-        reinterpret_cast<__nv_bfloat16*>(qkv), cos_t, sin_t, Hq, Hkv, Dh);
+    (void)actune::launch_pdl(rope_vec_kernel, dim3((unsigned)T), 256, 0, reinterpret_cast<cudaStream_t>(stream),
+        reinterpret_cast<__nv_bfloat16*>(qkv), cos_t, sin_t, Hq, Hkv, Dh, nullptr, 1, 0, 0);
     return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
   }
   const int64_t n = T * (Hq + Hkv) * (Dh / 2);
   (void)actune::launch_pdl(rope_kernel, dim3(grid_for(n)), 256, 0, reinterpret_cast<cudaStream_t>(stream), 
       reinterpret_cast<__nv_bfloat16*>(qkv), cos_t, sin_t, (int)T, Hq, Hkv, Dh);
+  return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
+}
+
+int actune_harness_rope_cache(void* qkv, const float* cos_t, const float* sin_t, int64_t T, int Hq, int Dh,
+                              void* cache, int64_t seq, int64_t Tc, int64_t offset, void* stream) {
+  if (T < 0 || Hq <= 0 || Dh <= 0 || (Dh / 2) % 8 || seq <= 0 || T % seq || offset < 0 || offset + seq > Tc ||
+      qkv == nullptr || cos_t == nullptr || sin_t == nullptr || cache == nullptr)
+    return ACTUNE_ERR_INVALID_VALUE;
+  if (T == 0) return ACTUNE_OK;
+  if (!aligned16(qkv) || !aligned16(cos_t) || !aligned16(sin_t) || !aligned16(cache)) return ACTUNE_ERR_MISALIGNED;
+  (void)actune::launch_pdl(rope_vec_kernel, dim3((unsigned)T), 256, 0, reinterpret_cast<cudaStream_t>(stream),
+      reinterpret_cast<__nv_bfloat16*>(qkv), cos_t, sin_t, Hq, 1, Dh, reinterpret_cast<__nv_bfloat16*>(cache),
+      (int)seq, (int)Tc, (int)offset);
   return cudaGetLastError() == cudaSuccess ? ACTUNE_OK : ACTUNE_ERR_CUDA;
 }
 

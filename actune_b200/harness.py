@@ -49,6 +49,8 @@ def _hlib():
         L.actune_harness_rmsnorm_q.restype = i32
         L.actune_harness_gated_act_q.argtypes = [p, p, i64, i64, i32, i32, i32, p, p, p]
         L.actune_harness_gated_act_q.restype = i32
+        L.actune_harness_rope_cache.argtypes = [p, p, p, i64, i32, i32, p, i64, i64, i64, p]
+        L.actune_harness_rope_cache.restype = i32
         _H = L
     return _H
 
@@ -91,6 +93,24 @@ def rope_(qkv, cos, sin, hq, hkv, dh):
     T = qkv.numel() // qkv.shape[-1]
     _lib.check(_hlib().actune_harness_rope(_p(qkv), _p(cos), _p(sin), T, hq, hkv, dh, _s(qkv)), "rope")
     return qkv
+
+
+def rope_cache_(qkv, cos, sin, hq, dh, cache, seq, offset):
+    """rope_ for one key/value head that also writes each token's rotated key and
+    its value into ``cache`` [B, Tc, 2, dh] at positions offset .. offset + seq - 1."""
+    T = qkv.numel() // qkv.shape[-1]
+    _lib.check(_hlib().actune_harness_rope_cache(_p(qkv), _p(cos), _p(sin), T, hq, dh, _p(cache), seq,
+                                                 _cache_pitch(cache, dh), offset, _s(qkv)), "rope_cache")
+    return qkv
+
+
+def _cache_pitch(cache, dh):
+    """Positions between consecutive sequences of a [B, T, 2, dh] cache view whose
+    rows are contiguous (a slice of a longer buffer keeps the buffer's pitch)."""
+    if cache.dim() != 4 or cache.shape[2:] != (2, dh) or cache.stride()[1:] != (2 * dh, dh, 1) or \
+            cache.stride(0) % (2 * dh):
+        raise ValueError("the cache must be [B, T, 2, head_dim] with contiguous rows")
+    return cache.stride(0) // (2 * dh) if cache.shape[0] > 1 else cache.shape[1]
 
 
 def gated_act(gu, gelu=False, quant_bits=None, codes8=False):
@@ -165,18 +185,19 @@ class DecoderLayer(torch.nn.Module):
         h, residual = rmsnorm(x, self.input_norm, self.eps, residual, self.gemma,
                               **input_format(self.qkv_proj, rows))
         qkv = self.qkv_proj(h)
-        rope_(qkv, cos, sin, self.heads, self.kv_heads, self.head_dim)
         qd, kvd = self.heads * self.head_dim, self.kv_heads * self.head_dim
-        q = qkv[:, :qd].view(B, T, self.heads, self.head_dim).transpose(1, 2)
         if cache is None:
+            rope_(qkv, cos, sin, self.heads, self.kv_heads, self.head_dim)
             k = qkv[:, qd:qd + kvd].view(B, T, self.kv_heads, self.head_dim).transpose(1, 2)
             v = qkv[:, qd + kvd:].view(B, T, self.kv_heads, self.head_dim).transpose(1, 2)
         else:
             if self.kv_heads != 1:
                 raise ValueError("the key/value cache holds one KV head")
-            cache[:, offset:offset + T].copy_(qkv[:, qd:].view(B, T, 2, self.head_dim))
+            # One launch rotates and writes the call's keys and values into the cache.
+            rope_cache_(qkv, cos, sin, self.heads, self.head_dim, cache, T, offset)
             k = cache[:, :offset + T, 0].unsqueeze(1)
             v = cache[:, :offset + T, 1].unsqueeze(1)
+        q = qkv[:, :qd].view(B, T, self.heads, self.head_dim).transpose(1, 2)
         attn = F.scaled_dot_product_attention(q, k, v, is_causal=causal and offset == 0,
                                               enable_gqa=self.kv_heads != self.heads)
         attn = attn.transpose(1, 2).reshape(rows, self.heads * self.head_dim)

@@ -46,6 +46,14 @@ int actune_harness_rmsnorm_q(const void* x, const void* residual, const void* we
 int actune_harness_gated_act_q(const void* gu, void* out, int64_t T, int64_t I, int gelu, int A, int codes8,
                                uint8_t* packed, float* scales, void* stream);
 
+/* actune_harness_rope for one key/value head (Hkv = 1, Dh/2 a multiple of 8,
+ * 16-byte aligned buffers) that also writes each token's rotated key and its value
+ * into a key/value cache of rows [.., 2, Dh], Tc positions apart between sequences:
+ * row b * seq + t of qkv goes to position offset + t of sequence b (T = B * seq
+ * rows, offset + seq <= Tc). */
+int actune_harness_rope_cache(void* qkv, const float* cos_t, const float* sin_t, int64_t T, int Hq, int Dh,
+                              void* cache, int64_t seq, int64_t Tc, int64_t offset, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -404,3 +404,22 @@ def test_graph_replay_literal_constants_and_shared_inputs():
     late.enabled = True
     with pytest.raises(RuntimeError, match="Unwarmed CUDA constant"):
         late(torch.ones(3, device="cuda"))
+
+
+def test_rope_cache_equals_rope_then_copy():
+    """The rotary kernel that also writes the call's keys and values into a cache
+    view whose sequences sit further apart than their length is bit-identical to the
+    rotation followed by the copy."""
+    from actune_b200 import harness as H
+    heads, dh, batch, seq, offset, pitch = 8, 256, 3, 50, 304, 354
+    g = torch.Generator(device="cuda").manual_seed(7)
+    qkv = torch.randn(batch * seq, (heads + 2) * dh, device="cuda", generator=g).bfloat16()
+    cos, sin = H.rope_tables(batch * seq, dh, 10000.0, "cuda")
+    for view_len in (pitch, offset + seq):
+        buf_a = torch.randn(batch, pitch, 2, dh, device="cuda", generator=g).bfloat16()
+        buf_b = buf_a.clone()
+        qa, qb = qkv.clone(), qkv.clone()
+        H.rope_(qa, cos, sin, heads, 1, dh)
+        buf_a[:, offset:offset + seq].copy_(qa[:, heads * dh:].view(batch, seq, 2, dh))
+        H.rope_cache_(qb, cos, sin, heads, dh, buf_b[:, :view_len], seq, offset)
+        assert torch.equal(qa, qb) and torch.equal(buf_a, buf_b)
