@@ -478,8 +478,17 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::TILE_THREADS, OCC)
     // accumulation of the previous half, and the first half of the next stage
     // is loaded before the last half of this one is accumulated.  Activation
     // scales are fetched two stages ahead into static register slots.
-    // Activation scales and the output may belong to the previous kernel.
-    if (p.pdl_wait) griddep_wait();
+    // Dependent launch: while the previous kernel finishes, pull this tile's first
+    // weight boxes into L2 (they never depend on it), so that the producer's first
+    // copies after the wait hit L2.  Activation scales and the output may belong to
+    // the previous kernel: wait for it before touching them.
+    if (p.pdl_wait) {
+      if (warp == C::EPI_WARP0 && lane == 0) {
+        const int pre = min(C::STAGES, n_iters);
+        for (int j = 0; j < pre; ++j) tma_prefetch_l2_2d(&tm_wgt, j * (C::KS * W / 8), n0);
+      }
+      griddep_wait();
+    }
     const int ew = warp - C::EPI_WARP0;
     const int q = warp & 3;      // TMEM lane quarter this warp may access
     const int e = ew >> 2;       // column slice
