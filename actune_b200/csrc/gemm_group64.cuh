@@ -546,6 +546,66 @@ __global__ void __launch_bounds__(Group64Cfg<W, A, BN, OCC>::TILE_THREADS, OCC)
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[pr]);
       }
+    } else if constexpr (!DOTS && C::COLS <= 32) {
+      // Narrow tiles (at most 32 columns per thread): the TMEM loads of NB whole
+      // stages are issued back to back and waited for once, their accumulator pairs
+      // released, then accumulated, so that a stage costs a fraction of one TMEM load
+      // latency instead of one latency per part; with NPAIR >= 2 * NB the MMA fills
+      // the next batch's pairs meanwhile.  Scales are fetched two batches ahead.
+      constexpr int NB = (C::COLS <= 16 && C::NPAIR >= 4) ? 2 : 1;
+      uint32_t r[NB][2][C::COLS];
+      float sc[NB][2], sn[NB][2], sn2[NB][2];
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          sc[b][h] = scale_at(2 * b + h);
+          sn[b][h] = scale_at(2 * (NB + b) + h);
+        }
+      for (int it = 0; it < n_iters && ok; it += NB) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) sn2[b][h] = scale_at(2 * (it + 2 * NB + b) + h);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          const int s = it + b;
+          if (s < n_iters) {
+            const int pr = s % C::NPAIR;
+            if (!mbar_wait(&acc_full[pr], (s / C::NPAIR) & 1, kSiteEpilogue)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            tmem_ld<C::COLS>(lane_base + pr * (2 * BN), r[b][0]);
+            tmem_ld<C::COLS>(lane_base + pr * (2 * BN) + BN, r[b][1]);
+          }
+        }
+        if (!ok) break;
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll
+          for (int b = 0; b < NB; ++b)
+            if (it + b < n_iters) mbar_arrive(&acc_empty[(it + b) % C::NPAIR]);
+        }
+        // Past the end of K (odd G) the second group's dots are 0 and so is its scale.
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          if (it + b < n_iters) {
+            accumulate<C::COLS>(acc, r[b][0], sc[b][0] * shift_scale);
+            accumulate<C::COLS>(acc, r[b][1], sc[b][1] * shift_scale);
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            sc[b][h] = sn[b][h];
+            sn[b][h] = sn2[b][h];
+          }
+      }
     } else {
       ok = mbar_wait(&acc_full[0], 0, kSiteEpilogue);
       if (ok) {
