@@ -185,6 +185,23 @@ def test_gemm_random_bit_exact(ops, w, a, m, k, n):
     assert_bits(bf16_bits(y), O.to_bf16_bits(ref), "bf16 output")
 
 
+@pytest.mark.parametrize("w", [2, 4, 8])
+@pytest.mark.parametrize("m", [1, 20, 33, 50, 57, 64])
+def test_gemm_single_token_tile(ops, w, m):
+    """One tile of at most 64 int8 token rows (a token box only as high as the tokens;
+    every tile width, the wave-tail split included): fp32 and bf16 outputs bit-exact
+    against the oracle, with and without bias, odd and even group counts, ragged N."""
+    for k, n, bias_dtype in [(448, 200, torch.bfloat16), (1024, 1000, None), (128, 12288, torch.float32),
+                             (256, 20480, None)]:
+        for variant in (0, 1, 2, 3):
+            seed = m + k + n + 10 * w + variant
+            y, ref, _ = _case(ops, m, k, n, w, 8, seed, bias_dtype=bias_dtype, out_dtype=torch.float32,
+                              variant=variant)
+            assert_bits(y.numpy(), ref, f"fp32 m={m} k={k} n={n} variant={variant}")
+    y, ref, _ = _case(ops, m, 4096, 2560, w, 8, seed=m + w, variant=1)
+    assert_bits(bf16_bits(y), O.to_bf16_bits(ref), f"bf16 output m={m} 4096x2560 BN32")
+
+
 @pytest.mark.parametrize("w,a", PAIRS)
 @pytest.mark.parametrize("variant", [9, 10, 11])
 def test_gemm_two_ctas_per_sm_variants(ops, w, a, variant):
