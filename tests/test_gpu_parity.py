@@ -236,6 +236,47 @@ def test_gemm_auto_split_waves(ops, w, a, m, k, n):
     assert torch.equal(auto, whole)
 
 
+@pytest.mark.parametrize("w,a", [(8, 8), (4, 8), (8, 4), (2, 2)])
+@pytest.mark.parametrize("m,k,n", [(300, 192, 136), (260, 1024, 256)])
+def test_gemm_extreme_codes_and_scales(ops, w, a, m, k, n):
+    """Raw codes at both ends of their range (|dot| up to 2^20, the largest an int8
+    group dot reaches), activation scales near 2^105 (products near 2^125), subnormal
+    and zero scales, an odd group count and a ragged N, over several token tiles:
+    fp32 and bf16 outputs bit-exact against the oracle for tile widths 128 and 64 and
+    AUTO."""
+    g = torch.Generator().manual_seed(m + k + n + 10 * w + a)
+    lo_a, hi_a = -(1 << (a - 1)), (1 << (a - 1)) - 1
+    lo_w, hi_w = -(1 << (w - 1)), (1 << (w - 1)) - 1
+    qa = torch.randint(lo_a, hi_a + 1, (m, k), generator=g, dtype=torch.int8)
+    qw = torch.randint(lo_w, hi_w + 1, (n, k), generator=g, dtype=torch.int8)
+    qa[0], qa[1], qa[2] = lo_a, hi_a, lo_a
+    qa[2, 1::2] = hi_a
+    qw[0], qw[1] = lo_w, hi_w
+    G = k // 64
+    as_ = torch.empty(m, G).uniform_(1e-3, 1e-1, generator=g)
+    as_[3, 0] = 2.0 ** 105                  # s * 2^23 overflows: conversion path
+    as_[4, 0] = 2.0 ** 104 * 1.9990234375   # largest kind of scale still carried
+    as_[5, :] = 2.0 ** 105                  # every group (odd ones keep the hardware conversion)
+    as_[5, 1:] = 1e-3
+    as_[6, :] = 1e-40                       # subnormal
+    as_[7, 0] = 0.0
+    as_[0, 0] = 2.0 ** 105                  # with the largest dot
+    ws = torch.empty(n).uniform_(1e-3, 2e-2, generator=g)
+    bias = torch.randn(n, generator=g) * 0.1
+    pa = ops.pack_rows(qa.to(DEV), a)
+    pw = ops.pack_rows(qw.to(DEV), w)
+    ref = O.packed_linear(pa.cpu().numpy(), as_.numpy(), pw.cpu().numpy(), ws.numpy(), bias.numpy(), k, w, a,
+                          fma=True)
+    assert np.isfinite(ref).all()
+    for variant in (3, 2, 0):  # BN128 (preset), BN64 (plain), AUTO
+        y = ops.packed_linear(pa, as_.to(DEV), pw, ws.to(DEV), bias.to(DEV), k, w, a, out_dtype=torch.float32,
+                              variant=variant)
+        assert_bits(y.cpu().numpy(), ref, f"fp32 variant {variant}")
+        yb = ops.packed_linear(pa, as_.to(DEV), pw, ws.to(DEV), bias.to(DEV), k, w, a, out_dtype=torch.bfloat16,
+                               variant=variant)
+        assert_bits(bf16_bits(yb), O.to_bf16_bits(ref), f"bf16 variant {variant}")
+
+
 @pytest.mark.parametrize("w,a", PAIRS)
 @pytest.mark.parametrize("variant", [12, 13])
 def test_gemm_persistent_variants(ops, w, a, variant):
