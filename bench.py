@@ -999,15 +999,104 @@ def config1(args):
                    "l2": "flushed before every call"},
         "cpu_baseline": {"value": round(total_cpu, 1), "unit": "us", "cores": cores, "kind": "port",
                          "sample": "every case once, the reference's dequantize-and-matmul formula"},
+        "native_pairs_us": round(sum(r["us"] for r in result["rows"] if (r["W"], r["A"]) in NATIVE_PAIRS), 1),
         "hbm_gbs": result["hbm_gbs"], "int8_tops": result["int8_tops"], "cases": result["rows"]}), flush=True)
+
+
+# The pairs the reference runs on its CUDA kernel (grouped_native.cu, W and A <= 4);
+# pairs with an 8-bit operand run its Triton kernel.
+NATIVE_PAIRS = ((2, 2), (2, 4), (4, 2), (4, 4))
+
+
+def graph_time_us(torch, fn, flush, reps=10):
+    """Per-call microseconds of fn() after an L2-evicting write: CUDA-graph replay of
+    [flush, call] x reps minus that of [flush] x reps, CUDA events on the capturing
+    stream, median of 5 replays."""
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        g_call, g_flush = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_call, stream=stream):
+            for _ in range(reps):
+                flush.zero_()
+                fn()
+        with torch.cuda.graph(g_flush, stream=stream):
+            for _ in range(reps):
+                flush.zero_()
+    torch.cuda.synchronize()
+
+    def replay(g):
+        ts = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3)
+        return statistics.median(ts)
+
+    us = (replay(g_call) - replay(g_flush)) / reps
+    del g_call, g_flush
+    return us
+
+
+def config1_reference(args):
+    """Reference arm of config 1: the reference's own GPU kernel for the pairs it
+    runs natively -- grouped_native.cu's linear() (warp-level mma.sync int4, built
+    from the reference's sources for sm_100a into oracle/_ref) -- on the config-1
+    shapes and token counts, timed exactly as this library's sweep (L2 flushed,
+    graph-replayed).  Its value is the sum over those 80 cases; this library's
+    config-1 line carries the same sum as `native_pairs_us`."""
+    import torch
+    from oracle import build_ref
+    ref = build_ref.load("ref_grouped_native")
+    if ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/ref_grouped_native was not built (the "
+                                                             "reference sources were absent at build time)"}))
+        return
+    dev = torch.device("cuda")
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    shapes = {"qkv": (4096, 12288), "o": (4096, 4096), "gate_up": (4096, 22016), "down": (11008, 4096)}
+    rows = []
+    for (w, a) in NATIVE_PAIRS:
+        for name, (k, n) in shapes.items():
+            g = torch.Generator(device=dev).manual_seed(1000 * w + 10 * a + k + n)
+            pw = torch.randint(0, 256, (n, k * w // 8), device=dev, dtype=torch.uint8, generator=g)
+            ws = torch.rand(n, device=dev, generator=g) * 0.01
+            bias = torch.empty(0, device=dev)
+            for m in (1, 8, 64, 256, 512):
+                pa = torch.randint(0, 256, (m, k * a // 8), device=dev, dtype=torch.uint8, generator=g)
+                as_ = torch.rand(m, k // 64, device=dev, generator=g) * 0.01
+                src = torch.empty(m, k, device=dev, dtype=torch.bfloat16)  # output dtype carrier
+                us = graph_time_us(torch, lambda: ref.linear(pa, as_, pw, ws, bias, src, w, a), flush)
+                rows.append({"W": w, "A": a, "shape": name, "M": m, "K": k, "N": n, "us": round(us, 2),
+                             "tops": round(2 * m * n * k / us / 1e6, 1)})
+    total = sum(r["us"] for r in rows)
+    print(json.dumps({
+        "impl": "reference", "metric": "us for the W{2,4}xA{2,4} cases of the config-1 sweep (sum over 80 cases)",
+        "value": round(total, 1), "unit": "us", "n_gpus": 1, "steps": 1, "warmup": 3, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4", "data": "synthetic (random packed operands)",
+        "config": {"workload": "config1 native pairs: W{2,4}xA{2,4} x {QKV, O, gate/up, down} x M in "
+                               "{1,8,64,256,512}", "l2": "flushed before every call"},
+        "kernel": "reference grouped_native.cu linear() (mma.sync m16n8k64 s4), built from its sources for sm_100a",
+        "e2e": {"value": round(total, 1), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cases": rows}), flush=True)
 
 
 def main():
     args = parse()
+    if args.config == 1 and args.impl == "reference":
+        config1_reference(args)
+        return
     if args.config in (0, 1):
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "configs 0 and 1 report their CPU formula inside "
-                                                                 "the line's cpu_baseline"}), flush=True)
+            print(json.dumps({"impl": "reference", "unavailable": "config 0 is W4A8, which the reference runs on its "
+                                                                 "Triton kernel (not built outside the reference "
+                                                                 "tree); its CPU formula is the line's cpu_baseline"}),
+                  flush=True)
             return
         (config0 if args.config == 0 else config1)(args)
         return
