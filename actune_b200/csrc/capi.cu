@@ -390,6 +390,13 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
       return cuda_status(e);
     }
   }
+  // AUTO with one token tile of int8 codes and a narrow weight tile: the four-group-
+  // stage kernel (same arithmetic, half the per-stage waits and commits per group).
+  if (variant == ACTUNE_VARIANT_AUTO && !wt && dots == nullptr && W == 8 && A == 8 && M <= 128 &&
+      (bn == 32 || bn == 64)) {
+    p.pdl_wait = 1;
+    return cuda_status(launch_group64_wide(bn, 4, ta, tw, p, stream));
+  }
   // The debug dots export always runs the one-CTA-per-SM form.  The one-CTA form is a
   // dependent launch: it prefetches its first weight tiles while the previous kernel
   // finishes.

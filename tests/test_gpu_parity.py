@@ -236,8 +236,31 @@ def test_gemm_auto_split_waves(ops, w, a, m, k, n):
     assert torch.equal(auto, whole)
 
 
+@pytest.mark.parametrize("m", [33, 50, 64, 100, 128])
+@pytest.mark.parametrize("k,n", [(64, 200), (192, 1000), (1088, 1024), (4096, 2560), (1024, 8192)])
+def test_gemm_four_group_stages(ops, m, k, n):
+    """AUTO on one token tile of int8 codes (W = A = 8, the decoded path every pair
+    takes above 32 token rows) with a 32- or 64-column tile runs the four-group-stage
+    kernel: 1, 3, 17, 64 and 16 groups (partial and whole last stages), ragged N, with
+    and without bias, three output types -- bit-exact against the oracle and identical
+    to the two-group-stage kernel (explicit BN32 and BN64)."""
+    for bias_dtype, out_dtype in [(torch.bfloat16, torch.bfloat16), (None, torch.float32),
+                                  (torch.float32, torch.float16)]:
+        seed = m + k + n + (0 if bias_dtype is None else 1)
+        y, ref, (pa, pw, pa_h) = _case(ops, m, k, n, 8, 8, seed, bias_dtype=bias_dtype, out_dtype=out_dtype)
+        if out_dtype == torch.float32:
+            assert_bits(y.numpy(), ref, f"fp32 m={m} k={k} n={n}")
+        elif out_dtype == torch.bfloat16:
+            assert_bits(bf16_bits(y), O.to_bf16_bits(ref), f"bf16 m={m} k={k} n={n}")
+        for variant in (1, 2):
+            y2, _, _ = _case(ops, m, k, n, 8, 8, seed, bias_dtype=bias_dtype, out_dtype=out_dtype, variant=variant)
+            assert torch.equal(y.view(torch.int16) if y.dtype != torch.float32 else y.view(torch.int32),
+                               y2.view(torch.int16) if y2.dtype != torch.float32 else y2.view(torch.int32)), \
+                f"AUTO vs variant {variant} m={m} k={k} n={n} {out_dtype}"
+
+
 @pytest.mark.parametrize("w,a", [(8, 8), (4, 8), (8, 4), (2, 2)])
-@pytest.mark.parametrize("m,k,n", [(300, 192, 136), (260, 1024, 256)])
+@pytest.mark.parametrize("m,k,n", [(300, 192, 136), (260, 1024, 256), (50, 192, 136), (100, 1088, 2560)])
 def test_gemm_extreme_codes_and_scales(ops, w, a, m, k, n):
     """Raw codes at both ends of their range (|dot| up to 2^20, the largest an int8
     group dot reaches), activation scales near 2^105 (products near 2^125), subnormal
