@@ -390,10 +390,10 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
       return cuda_status(e);
     }
   }
-  // AUTO with one token tile of int8 codes and a narrow weight tile: the four-group-
-  // stage kernel (same arithmetic, half the per-stage waits and commits per group).
-  if (variant == ACTUNE_VARIANT_AUTO && !wt && dots == nullptr && W == 8 && A == 8 && M <= 128 &&
-      (bn == 32 || bn == 64)) {
+  // AUTO on int8 codes with a narrow weight tile (few token tiles, narrow outputs): the
+  // four-group-stage kernel (same arithmetic, half the per-stage waits and commits per
+  // group).  The explicit BN32 / BN64 variants keep the two-group-stage kernel.
+  if (variant == ACTUNE_VARIANT_AUTO && !wt && dots == nullptr && W == 8 && A == 8 && (bn == 32 || bn == 64)) {
     p.pdl_wait = 1;
     return cuda_status(launch_group64_wide(bn, 4, ta, tw, p, stream));
   }

@@ -1,21 +1,21 @@
-// Group-64 tile GEMM with four-group stages, for one token tile (M <= 128) of int8
-// codes (W = A = 8: the decoded-code path every pair takes above 32 token rows) and
-// narrow weight tiles (32 or 64 rows).
+// Group-64 tile GEMM with four-group stages for int8 codes (W = A = 8: the
+// decoded-code path every pair takes above 32 token rows) and narrow weight tiles
+// (32 or 64 rows), which AUTO picks for few token tiles and narrow outputs.
 //
 // Same arithmetic as group64_gemm_kernel (gemm_group64.cuh): exact int32 dots per
 // 64-group on tcgen05 kind::i8, then acc = fma(float(dot_g), as[m, g], acc) for
 // g = 0, 1, ... in order and y = fma(acc, ws[n], bias[n]) (or acc * ws[n]), rounded
 // once (actune/kernels/grouped.py:80-94, actune/kernels/grouped_native.cu:70-85).
 //
-// Why a separate kernel: with a single token tile the K loop of one CTA is the whole
+// Why a separate kernel: with few token tiles the K loop of one CTA is the whole
 // critical path, and per stage it pays a fixed cost besides its MMAs -- the operand
 // and accumulator waits, one commit for the accumulators and one for the ring slot,
 // each holding the issuing thread about as long as an MMA.  A stage of 256 K (four
 // groups, 8 MMAs) pays that cost once per four groups instead of once per two.
 //
 // Layout: a stage holds each operand as K/128 column blocks of 128-byte rows in the
-// canonical 128-byte-swizzled K-major layout (token blocks 128 rows, of which the
-// token box fills the first M rounded up to 8; weight blocks BN rows).  Tensor memory
+// canonical 128-byte-swizzled K-major layout (token blocks 128 rows, of which a
+// single tile's token box fills the first M rounded up to 8; weight blocks BN rows).  Tensor memory
 // holds NSET sets of GS accumulators of BN int32 columns.  Roles: warp 0 producer
 // (lanes 0..KB-1 the token blocks, lanes KB..2KB-1 the weight blocks of a stage, one
 // instruction), warps 1 and 10 MMA issuers (even and odd stages: one issuing thread is
@@ -364,7 +364,7 @@ static cudaError_t launch_wide_t(const CUtensorMap& ta, const CUtensorMap& tw, c
 
 cudaError_t launch_group64_wide(int bn, int gs, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
                                 cudaStream_t stream) {
-  if (p.M > 128 || p.dots != nullptr) return cudaErrorInvalidValue;
+  if (p.dots != nullptr) return cudaErrorInvalidValue;
   if (bn == 32) return gs == 8 ? launch_wide_t<32, 8>(ta, tw, p, stream) : launch_wide_t<32, 4>(ta, tw, p, stream);
   if (bn == 64) return launch_wide_t<64, 4>(ta, tw, p, stream);
   return cudaErrorInvalidValue;

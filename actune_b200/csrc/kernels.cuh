@@ -35,9 +35,9 @@ cudaError_t launch_gemv_tokenwise(int W, int A, const CUtensorMap& ta, const CUt
 constexpr int kGemvRows = 32;
 cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap* ts,
                                 const GemmParams& p, int num_sms, cudaStream_t stream);
-// Four-group-stage tile GEMM (gemm_wide.cu): int8 codes (W = A = 8), one token tile
-// (M <= 128), weight tiles of bn = 32 or 64 rows, gs = 4 (or 8 at bn = 32) groups per
-// stage, group-64 outputs only.  Maps as for the tile GEMM with 128-byte boxes.
+// Four-group-stage tile GEMM (gemm_wide.cu): int8 codes (W = A = 8), weight tiles of
+// bn = 32 or 64 rows, gs = 4 (or 8 at bn = 32) groups per stage, group-64 outputs
+// only.  Maps as for the tile GEMM with 128-byte boxes.
 cudaError_t launch_group64_wide(int bn, int gs, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
                                 cudaStream_t stream);
 cudaError_t launch_pack_rows(const int8_t* q, int64_t total_bytes, int bits, uint8_t* packed, int num_sms,

@@ -236,14 +236,14 @@ def test_gemm_auto_split_waves(ops, w, a, m, k, n):
     assert torch.equal(auto, whole)
 
 
-@pytest.mark.parametrize("m", [33, 50, 64, 100, 128])
+@pytest.mark.parametrize("m", [33, 50, 64, 100, 128, 200, 304])
 @pytest.mark.parametrize("k,n", [(64, 200), (192, 1000), (1088, 1024), (4096, 2560), (1024, 8192)])
 def test_gemm_four_group_stages(ops, m, k, n):
-    """AUTO on one token tile of int8 codes (W = A = 8, the decoded path every pair
-    takes above 32 token rows) with a 32- or 64-column tile runs the four-group-stage
-    kernel: 1, 3, 17, 64 and 16 groups (partial and whole last stages), ragged N, with
-    and without bias, three output types -- bit-exact against the oracle and identical
-    to the two-group-stage kernel (explicit BN32 and BN64)."""
+    """AUTO on int8 codes (W = A = 8, the decoded path every pair takes above 32 token
+    rows) with a 32- or 64-column tile runs the four-group-stage kernel: one to three
+    token tiles, 1, 3, 17, 64 and 16 groups (partial and whole last stages), ragged N,
+    with and without bias, three output types -- bit-exact against the oracle and
+    identical to the two-group-stage kernel (explicit BN32 and BN64)."""
     for bias_dtype, out_dtype in [(torch.bfloat16, torch.bfloat16), (None, torch.float32),
                                   (torch.float32, torch.float16)]:
         seed = m + k + n + (0 if bias_dtype is None else 1)
