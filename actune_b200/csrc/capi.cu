@@ -386,7 +386,11 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
       pa.n_end = (int)(na * 128);
       pb.n_base = (int)(na * 128);
       cudaError_t e = dispatch_gemm(W, A, 128, false, ta, tw, pa, stream);
-      if (e == cudaSuccess) e = dispatch_gemm(W, A, bn_b, false, ta, tw_b, pb, stream, true);
+      // The narrow tail tiles of int8 codes run the four-group-stage form (a dependent
+      // launch like the two-group one).
+      if (e == cudaSuccess)
+        e = (W == 8 && A == 8) ? launch_group64_wide(bn_b, 4, ta, tw_b, pb, stream)
+                               : dispatch_gemm(W, A, bn_b, false, ta, tw_b, pb, stream, true);
       return cuda_status(e);
     }
   }
