@@ -443,8 +443,11 @@ def sample_pi05(model, prefix_call, step_call, embeds, noise, state=None):
     `prefix_call` / `step_call` are the model's prefix / denoise_step, or their
     graph-replayed wrappers (one CUDA graph per step shape)."""
     prefix_call(embeds)
-    dt = torch.tensor(-1.0 / model.steps, dtype=torch.float32, device=noise.device)
-    time = torch.tensor(1.0, dtype=torch.float32, device=noise.device)
+    # The same float32 values as torch.tensor(-1 / steps) and torch.tensor(1.0), made
+    # by fill kernels: a tensor built from a host scalar is a blocking host-to-device
+    # copy, which would stall the host here until the prefix has run.
+    dt = torch.full((), -1.0 / model.steps, dtype=torch.float32, device=noise.device)
+    time = torch.full((), 1.0, dtype=torch.float32, device=noise.device)
     x_t = noise
     for _ in range(model.steps):
         x_t, time = step_call(x_t, time, dt) if state is None else step_call(x_t, time, dt, state)
