@@ -386,20 +386,21 @@ int run_gemm(const uint8_t* a, const float* a_scale, const uint8_t* w, const flo
       pa.n_end = (int)(na * 128);
       pb.n_base = (int)(na * 128);
       cudaError_t e = dispatch_gemm(W, A, 128, false, ta, tw, pa, stream);
-      // The narrow tail tiles of int8 codes run the four-group-stage form (a dependent
-      // launch like the two-group one).
+      // The narrow tail tiles run the four-group-stage form (a dependent launch like
+      // the two-group one).
       if (e == cudaSuccess)
-        e = (W == 8 && A == 8) ? launch_group64_wide(bn_b, 4, ta, tw_b, pb, stream)
-                               : dispatch_gemm(W, A, bn_b, false, ta, tw_b, pb, stream, true);
+        e = group64_wide_preferred(W, A, bn_b) ? launch_group64_wide(W, A, bn_b, 4, ta, tw_b, pb, stream)
+                                               : dispatch_gemm(W, A, bn_b, false, ta, tw_b, pb, stream, true);
       return cuda_status(e);
     }
   }
-  // AUTO on int8 codes with a narrow weight tile (few token tiles, narrow outputs): the
-  // four-group-stage kernel (same arithmetic, half the per-stage waits and commits per
-  // group).  The explicit BN32 / BN64 variants keep the two-group-stage kernel.
-  if (variant == ACTUNE_VARIANT_AUTO && !wt && dots == nullptr && W == 8 && A == 8 && (bn == 32 || bn == 64)) {
+  // AUTO with a narrow weight tile (few token tiles, narrow outputs): the four-group-
+  // stage kernel (same arithmetic, half the per-stage waits and commits per group).
+  // The explicit BN32 / BN64 variants keep the two-group-stage kernel.
+  if (variant == ACTUNE_VARIANT_AUTO && !wt && dots == nullptr && (bn == 32 || bn == 64) &&
+      group64_wide_preferred(W, A, bn)) {
     p.pdl_wait = 1;
-    return cuda_status(launch_group64_wide(bn, 4, ta, tw, p, stream));
+    return cuda_status(launch_group64_wide(W, A, bn, 4, ta, tw, p, stream));
   }
   // The debug dots export always runs the one-CTA-per-SM form.  The one-CTA form is a
   // dependent launch: it prefetches its first weight tiles while the previous kernel

@@ -1,6 +1,8 @@
-// Group-64 tile GEMM with four-group stages for int8 codes (W = A = 8: the
-// decoded-code path every pair takes above 32 token rows) and narrow weight tiles
-// (32 or 64 rows), which AUTO picks for few token tiles and narrow outputs.
+// Group-64 tile GEMM with four-group stages for narrow weight tiles (32 or 64 rows),
+// which AUTO picks for few token tiles and narrow outputs, for every W x A pair:
+// int8 codes (W = A = 8, the decoded-code path) load straight into the operand
+// layout, packed sub-byte codes through a staging area that four converter warps
+// expand to int8 (code in the top bits of the byte, as in gemm_group64.cuh).
 //
 // Same arithmetic as group64_gemm_kernel (gemm_group64.cuh): exact int32 dots per
 // 64-group on tcgen05 kind::i8, then acc = fma(float(dot_g), as[m, g], acc) for
@@ -18,16 +20,19 @@
 // single tile's token box fills the first M rounded up to 8; weight blocks BN rows).  Tensor memory
 // holds NSET sets of GS accumulators of BN int32 columns.  Roles: warp 0 producer
 // (lanes 0..KB-1 the token blocks, lanes KB..2KB-1 the weight blocks of a stage, one
-// instruction), warps 1 and 10 MMA issuers (even and odd stages: one issuing thread is
-// held for each MMA's duration, so one issuer's waits and commits overlap the other's
-// MMAs), warps 2-9 epilogue (one token row and BN/2 columns per thread).  Every wait
-// is bounded (common.cuh: mbar_wait records ACTUNE_DEV_TIMEOUT and returns false).
+// instruction), warp 1 and the last warp MMA issuers (even and odd stages: one issuing
+// thread is held for each MMA's duration, so one issuer's waits and commits overlap the
+// other's MMAs), with sub-byte operands four converter warps, then eight epilogue warps
+// (one token row and BN/2 columns per thread).  Every wait is bounded (common.cuh:
+// mbar_wait records ACTUNE_DEV_TIMEOUT and returns false).
 #include "kernels.cuh"
 
 namespace actune {
 
-template <int BN, int GS>
+template <int W, int A, int BN, int GS>
 struct WideCfg {
+  static_assert(W == 2 || W == 4 || W == 8, "W");
+  static_assert(A == 2 || A == 4 || A == 8, "A");
   static_assert(BN == 32 || BN == 64, "narrow weight tiles");
   static_assert(GS == 4 || GS == 8, "groups per stage");
   static constexpr int BM = 128;                  // MMA M = TMEM lanes
@@ -41,16 +46,26 @@ struct WideCfg {
   static constexpr int A_BLK_BYTES = BM * 128;
   static constexpr int W_BLK_BYTES = BN * 128;
   static constexpr int OP_A_BYTES = KB * A_BLK_BYTES;
-  static constexpr int STAGE_BYTES = OP_A_BYTES + KB * W_BLK_BYTES;  // a multiple of 1024
+  static constexpr int OP_W_BYTES = KB * W_BLK_BYTES;
+  // Packed sub-byte codes of a 128-K block: rows of 16 * bits bytes, unswizzled.
+  static constexpr bool CONVERT = (A < 8) || (W < 8);
+  static constexpr int STG_A_BLK = A < 8 ? BM * 16 * A : 0;
+  static constexpr int STG_W_BLK = W < 8 ? BN * 16 * W : 0;
+  static constexpr int STG_A_OFF = OP_A_BYTES + OP_W_BYTES;
+  static constexpr int STG_W_OFF = STG_A_OFF + KB * STG_A_BLK;
+  static constexpr int STAGE_RAW = STG_W_OFF + KB * STG_W_BLK;
+  static constexpr int STAGE_BYTES = (STAGE_RAW + 1023) / 1024 * 1024;
   static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
-  // A multiple of NSET (a ring slot's accumulator set is a compile-time constant and
-  // slots and sets of one issuer coincide).
-  static constexpr int STAGES = (STAGES_FIT > 8 ? 8 : STAGES_FIT) / NSET * NSET;
+  // Even: each issuer owns every second ring slot (its descriptors stay in registers).
+  static constexpr int STAGES = (STAGES_FIT > 8 ? 8 : STAGES_FIT) / 2 * 2;
   static_assert(STAGES >= 2, "ring depth");
+  // int8 operand value = code * 2^(8 - bits): a dot carries 2^SHIFT.
+  static constexpr int SHIFT = (8 - A) + (8 - W);
   static constexpr int OUT_STAGE_BYTES = BM * (BN + 4) * 4;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES > OUT_STAGE_BYTES ? STAGES * STAGE_BYTES : OUT_STAGE_BYTES;
   static constexpr int SMEM_BYTES = RING_BYTES + 1024;
-  static constexpr int EPI_WARP0 = 2;
+  static constexpr int CVT_WARPS = CONVERT ? 4 : 0;
+  static constexpr int EPI_WARP0 = 2 + CVT_WARPS;
   static constexpr int EPI_WARPS = 4 * EPI_WG;
   static constexpr int MMA2_WARP = EPI_WARP0 + EPI_WARPS;
   static constexpr int THREADS = 32 * (MMA2_WARP + 1);
@@ -59,13 +74,14 @@ struct WideCfg {
   static_assert(GS % HG == 0, "whole waits per stage");
 };
 
-template <int BN, int GS>
-__global__ void __launch_bounds__(WideCfg<BN, GS>::THREADS, 1)
+template <int W, int A, int BN, int GS>
+__global__ void __launch_bounds__(WideCfg<W, A, BN, GS>::THREADS, 1)
     group64_wide_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_wgt,
                         const GemmParams p) {
-  using C = WideCfg<BN, GS>;
+  using C = WideCfg<W, A, BN, GS>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];  // the stage's copies landed
+  __shared__ __align__(8) uint64_t full_op[C::STAGES];   // converter warps done (sub-byte operands)
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
   __shared__ __align__(8) uint64_t acc_full[C::NSET];
   __shared__ __align__(8) uint64_t acc_empty[C::NSET];
@@ -85,6 +101,7 @@ __global__ void __launch_bounds__(WideCfg<BN, GS>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
+      mbar_init(&full_op[s], C::CVT_WARPS > 0 ? C::CVT_WARPS : 1);
       mbar_init(&empty_bar[s], 1);
     }
     for (int b = 0; b < C::NSET; ++b) {
@@ -113,14 +130,19 @@ __global__ void __launch_bounds__(WideCfg<BN, GS>::THREADS, 1)
     // One bulk-tensor instruction per stage: lane b < KB copies token block b, lane
     // KB + b weight block b.  Every operand of a copy sits in a register of its own
     // (a copy reads its register operands some time after issue).
+    // Packed operands: a 128-K block is a box of 16 * bits bytes per row into the
+    // staging area; int8 codes: 128 bytes per row straight into the operand block.
     int issued = 0;
-    const uint32_t tx_bytes = (uint32_t)C::KB * (uint32_t)(p.a_box_rows * 128 + BN * 128);
+    const uint32_t tx_bytes = (uint32_t)C::KB * (uint32_t)(p.a_box_rows * 16 * A + BN * 16 * W);
     if (lane < 2 * C::KB) {
       const bool is_a = lane < C::KB;
       const int blk = is_a ? lane : lane - C::KB;
       const CUtensorMap* map = is_a ? &tm_act : &tm_wgt;
       const int y = is_a ? m0 : n0;
-      const uint32_t dst_off = is_a ? blk * C::A_BLK_BYTES : C::OP_A_BYTES + blk * C::W_BLK_BYTES;
+      const int bits = is_a ? A : W;
+      const uint32_t dst_off = is_a ? (A < 8 ? C::STG_A_OFF + blk * C::STG_A_BLK : blk * C::A_BLK_BYTES)
+                                    : (W < 8 ? C::STG_W_OFF + blk * C::STG_W_BLK : C::OP_A_BYTES + blk * C::W_BLK_BYTES);
+      const int x_step = C::KS * bits / 8, x_blk = blk * 16 * bits;
       constexpr int S = C::STAGES, HALF = C::STAGES / 2;
       uint32_t dst[S], bar[S];
       int xs[S];
@@ -128,7 +150,7 @@ __global__ void __launch_bounds__(WideCfg<BN, GS>::THREADS, 1)
       for (int j = 0; j < S; ++j) {
         dst[j] = smem_u32(smem + j * C::STAGE_BYTES + dst_off);
         bar[j] = smem_u32(&full_bar[j]);
-        xs[j] = j * C::KS + blk * 128;
+        xs[j] = j * x_step + x_blk;
       }
       // Dependent launch: the tiles are requested once the previous kernel completed.
       if (p.pdl_wait) griddep_wait();
@@ -148,10 +170,10 @@ __global__ void __launch_bounds__(WideCfg<BN, GS>::THREADS, 1)
             ok = false;
             break;
           }
-          if (j + HALF < S) xs[j + HALF] = (it0 + j + HALF) * C::KS + blk * 128;
+          if (j + HALF < S) xs[j + HALF] = (it0 + j + HALF) * x_step + x_blk;
           tma_load_2d_u32(dst[j], map, xs[j], y, bar[j]);
           ++issued;
-          if (j >= HALF) xs[j - HALF] = (it0 + S + j - HALF) * C::KS + blk * 128;
+          if (j >= HALF) xs[j - HALF] = (it0 + S + j - HALF) * x_step + x_blk;
         }
         ph ^= 1;
       }
@@ -192,8 +214,8 @@ __global__ void __launch_bounds__(WideCfg<BN, GS>::THREADS, 1)
           for (int j = PAR; j < S; j += 2) {
             const int it = it0 + j;
             if (it >= n_iters) break;
-            const int set = j % C::NSET, u = j / 2;
-            if (!mbar_wait(&full_bar[j], ph, kSiteMmaFull) ||
+            const int set = it % C::NSET, u = j / 2;
+            if (!mbar_wait(C::CONVERT ? &full_op[j] : &full_bar[j], ph, kSiteMmaFull) ||
                 !mbar_wait(&acc_empty[set], ((it / C::NSET) & 1) ^ 1, kSiteMmaAcc)) {
               ok = false;
               break;
@@ -218,6 +240,33 @@ __global__ void __launch_bounds__(WideCfg<BN, GS>::THREADS, 1)
       mma_commit(&mma_done[who]);
       mbar_wait(&mma_done[who], 0, kSiteMmaDone);
     }
+  } else if (warp < C::EPI_WARP0) {
+    // ------------------------------------------------------------ converters
+    // Sub-byte codes of each 128-K block -> int8 in the canonical SW128 K-major layout
+    // (token rows past the last token are left as they are: they reach only
+    // accumulator rows that are never stored).
+    if constexpr (C::CONVERT) {
+      const int ctid = threadIdx.x - 64;
+      constexpr int NT = 32 * C::CVT_WARPS;
+      const int a_rows_valid = min(C::BM, p.M - m0);
+      for (int it = 0; it < n_iters; ++it) {
+        const int s = it % C::STAGES;
+        if (!mbar_wait(&full_bar[s], (it / C::STAGES) & 1, kSiteConverter)) break;
+        uint8_t* st = smem + s * C::STAGE_BYTES;
+#pragma unroll
+        for (int b = 0; b < C::KB; ++b) {
+          if constexpr (A < 8)
+            unpack_stage<A, C::BM, NT>(st + C::STG_A_OFF + b * C::STG_A_BLK, st + b * C::A_BLK_BYTES, ctid,
+                                       a_rows_valid);
+          if constexpr (W < 8)
+            unpack_stage<W, BN, NT>(st + C::STG_W_OFF + b * C::STG_W_BLK, st + C::OP_A_BYTES + b * C::W_BLK_BYTES,
+                                    ctid);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_op[s]);
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     // Dependent launch: while the previous kernel finishes, pull this tile's first
@@ -227,7 +276,7 @@ __global__ void __launch_bounds__(WideCfg<BN, GS>::THREADS, 1)
       if (warp == C::EPI_WARP0 && lane == 0) {
         const int pre = min(C::STAGES, n_iters);
         for (int j = 0; j < pre; ++j)
-          for (int b = 0; b < C::KB; ++b) tma_prefetch_l2_2d(&tm_wgt, j * C::KS + b * 128, n0);
+          for (int b = 0; b < C::KB; ++b) tma_prefetch_l2_2d(&tm_wgt, j * (C::KS * W / 8) + b * 16 * W, n0);
       }
       griddep_wait();
     }
@@ -243,7 +292,12 @@ __global__ void __launch_bounds__(WideCfg<BN, GS>::THREADS, 1)
     float2 acc[C::COLS / 2];
 #pragma unroll
     for (int j = 0; j < C::COLS / 2; ++j) acc[j] = make_float2(0.f, 0.f);
-    auto scale_at = [&](int g) -> float { return (load_scales && g < G) ? __ldg(as_row + g) : 0.f; };
+    // Scales carry 2^-SHIFT (exact: a power of two) for the top-bit placement of
+    // sub-byte codes; 1 for int8 codes.
+    const float shift_scale = 1.0f / float(1 << C::SHIFT);
+    auto scale_at = [&](int g) -> float {
+      return (load_scales && g < G) ? __ldg(as_row + g) * shift_scale : 0.f;
+    };
     bool ok = true;
     if (!warp_live) {
       // No valid token row in this warp: only keep the accumulator handshake.
@@ -350,11 +404,11 @@ __global__ void __launch_bounds__(WideCfg<BN, GS>::THREADS, 1)
   if (threadIdx.x == 0) griddep_wait();
 }
 
-template <int BN, int GS>
+template <int W, int A, int BN, int GS>
 static cudaError_t launch_wide_t(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
                                  cudaStream_t stream) {
-  using C = WideCfg<BN, GS>;
-  constexpr auto kernel = group64_wide_kernel<BN, GS>;
+  using C = WideCfg<W, A, BN, GS>;
+  constexpr auto kernel = group64_wide_kernel<W, A, BN, GS>;
   const cudaError_t e = ensure_smem_limit<kernel>(C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   const int n_end = p.n_end > 0 ? p.n_end : p.N;
@@ -362,11 +416,41 @@ static cudaError_t launch_wide_t(const CUtensorMap& ta, const CUtensorMap& tw, c
   return launch_pdl(kernel, grid, C::THREADS, C::SMEM_BYTES, stream, ta, tw, p);
 }
 
-cudaError_t launch_group64_wide(int bn, int gs, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
-                                cudaStream_t stream) {
+template <int W, int A>
+static cudaError_t launch_wide_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
+                                  cudaStream_t stream) {
+  if (bn == 32) return launch_wide_t<W, A, 32, 4>(ta, tw, p, stream);
+  if (bn == 64) return launch_wide_t<W, A, 64, 4>(ta, tw, p, stream);
+  return cudaErrorInvalidValue;
+}
+
+template <int W, int A>
+static bool wide_deep_ring(int bn) {
+  return bn == 32 ? WideCfg<W, A, 32, 4>::STAGES >= 4 : bn == 64 ? WideCfg<W, A, 64, 4>::STAGES >= 4 : false;
+}
+
+bool group64_wide_preferred(int W, int A, int bn) {
+#define ACTUNE_CASE(WW, AA) \
+  if (W == WW && A == AA) return wide_deep_ring<WW, AA>(bn);
+  ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
+  ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
+  ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
+#undef ACTUNE_CASE
+  return false;
+}
+
+cudaError_t launch_group64_wide(int W, int A, int bn, int gs, const CUtensorMap& ta, const CUtensorMap& tw,
+                                const GemmParams& p, cudaStream_t stream) {
   if (p.dots != nullptr) return cudaErrorInvalidValue;
-  if (bn == 32) return gs == 8 ? launch_wide_t<32, 8>(ta, tw, p, stream) : launch_wide_t<32, 4>(ta, tw, p, stream);
-  if (bn == 64) return launch_wide_t<64, 4>(ta, tw, p, stream);
+  if (gs == 8) return (W == 8 && A == 8 && bn == 32) ? launch_wide_t<8, 8, 32, 8>(ta, tw, p, stream)
+                                                     : cudaErrorInvalidValue;
+  if (gs != 4) return cudaErrorInvalidValue;
+#define ACTUNE_CASE(WW, AA) \
+  if (W == WW && A == AA) return launch_wide_bn<WW, AA>(bn, ta, tw, p, stream);
+  ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)
+  ACTUNE_CASE(4, 2) ACTUNE_CASE(4, 4) ACTUNE_CASE(4, 8)
+  ACTUNE_CASE(8, 2) ACTUNE_CASE(8, 4) ACTUNE_CASE(8, 8)
+#undef ACTUNE_CASE
   return cudaErrorInvalidValue;
 }
 

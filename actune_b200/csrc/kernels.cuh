@@ -35,11 +35,17 @@ cudaError_t launch_gemv_tokenwise(int W, int A, const CUtensorMap& ta, const CUt
 constexpr int kGemvRows = 32;
 cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap* ts,
                                 const GemmParams& p, int num_sms, cudaStream_t stream);
-// Four-group-stage tile GEMM (gemm_wide.cu): int8 codes (W = A = 8), weight tiles of
-// bn = 32 or 64 rows, gs = 4 (or 8 at bn = 32) groups per stage, group-64 outputs
-// only.  Maps as for the tile GEMM with 128-byte boxes.
-cudaError_t launch_group64_wide(int bn, int gs, const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p,
-                                cudaStream_t stream);
+// Four-group-stage tile GEMM (gemm_wide.cu): every W x A pair, weight tiles of bn = 32
+// or 64 rows, gs = 4 groups per stage (8 also built for W = A = 8 at bn = 32),
+// group-64 outputs only.  The same maps as the tile GEMM (int8 rows: 128-byte SW128
+// boxes; packed rows: unswizzled boxes of 16 * bits bytes).
+cudaError_t launch_group64_wide(int W, int A, int bn, int gs, const CUtensorMap& ta, const CUtensorMap& tw,
+                                const GemmParams& p, cudaStream_t stream);
+// Whether AUTO runs the four-group-stage form for this pair and tile width: when its
+// shared-memory ring holds at least four stages (int8 codes at 32 and 64 columns; at
+// 32 columns also W4A8, W2A8, W8A2, W2A2).  Packed activation staging leaves the other
+// forms two-stage rings, measured slower than the two-group-stage kernel.
+bool group64_wide_preferred(int W, int A, int bn);
 cudaError_t launch_pack_rows(const int8_t* q, int64_t total_bytes, int bits, uint8_t* packed, int num_sms,
                              cudaStream_t stream);
 

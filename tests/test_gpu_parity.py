@@ -259,6 +259,24 @@ def test_gemm_four_group_stages(ops, m, k, n):
                 f"AUTO vs variant {variant} m={m} k={k} n={n} {out_dtype}"
 
 
+@pytest.mark.parametrize("w,a", [p for p in PAIRS if p != (8, 8)])
+@pytest.mark.parametrize("m", [50, 200])
+@pytest.mark.parametrize("k,n", [(192, 1000), (1088, 264), (1024, 2560)])
+def test_gemm_four_group_stages_packed(ops, w, a, m, k, n):
+    """AUTO on packed sub-byte codes with a 32- or 64-column tile: the four-group-stage
+    kernel with its converter warps (packed codes expanded to int8 in shared memory)
+    where its ring holds four stages (W2A2, W2A8, W4A8, W8A2 at 32 columns), the
+    two-group-stage kernel otherwise -- bit-exact against the oracle and identical to
+    the explicit BN32 / BN64 variants, odd and even group counts, one and two token
+    tiles."""
+    seed = m + k + n + 10 * w + a
+    y, ref, _ = _case(ops, m, k, n, w, a, seed, out_dtype=torch.float32)
+    assert_bits(y.numpy(), ref, f"fp32 W{w}A{a} m={m} k={k} n={n}")
+    for variant in (1, 2):
+        y2, _, _ = _case(ops, m, k, n, w, a, seed, out_dtype=torch.float32, variant=variant)
+        assert torch.equal(y.view(torch.int32), y2.view(torch.int32)), f"AUTO vs variant {variant}"
+
+
 @pytest.mark.parametrize("w,a", [(8, 8), (4, 8), (8, 4), (2, 2)])
 @pytest.mark.parametrize("m,k,n", [(300, 192, 136), (260, 1024, 256), (50, 192, 136), (100, 1088, 2560)])
 def test_gemm_extreme_codes_and_scales(ops, w, a, m, k, n):
