@@ -441,10 +441,7 @@ bool group64_wide_preferred(int W, int A, int bn) {
 
 cudaError_t launch_group64_wide(int W, int A, int bn, int gs, const CUtensorMap& ta, const CUtensorMap& tw,
                                 const GemmParams& p, cudaStream_t stream) {
-  if (p.dots != nullptr) return cudaErrorInvalidValue;
-  if (gs == 8) return (W == 8 && A == 8 && bn == 32) ? launch_wide_t<8, 8, 32, 8>(ta, tw, p, stream)
-                                                     : cudaErrorInvalidValue;
-  if (gs != 4) return cudaErrorInvalidValue;
+  if (p.dots != nullptr || gs != 4) return cudaErrorInvalidValue;
 #define ACTUNE_CASE(WW, AA) \
   if (W == WW && A == AA) return launch_wide_bn<WW, AA>(bn, ta, tw, p, stream);
   ACTUNE_CASE(2, 2) ACTUNE_CASE(2, 4) ACTUNE_CASE(2, 8)

@@ -36,8 +36,8 @@ constexpr int kGemvRows = 32;
 cudaError_t launch_gemv_group64(int W, int A, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap* ts,
                                 const GemmParams& p, int num_sms, cudaStream_t stream);
 // Four-group-stage tile GEMM (gemm_wide.cu): every W x A pair, weight tiles of bn = 32
-// or 64 rows, gs = 4 groups per stage (8 also built for W = A = 8 at bn = 32),
-// group-64 outputs only.  The same maps as the tile GEMM (int8 rows: 128-byte SW128
+// or 64 rows, gs = 4 groups per stage (other values are refused), group-64 outputs
+// only.  The same maps as the tile GEMM (int8 rows: 128-byte SW128
 // boxes; packed rows: unswizzled boxes of 16 * bits bytes).
 cudaError_t launch_group64_wide(int W, int A, int bn, int gs, const CUtensorMap& ta, const CUtensorMap& tw,
                                 const GemmParams& p, cudaStream_t stream);
