@@ -16,9 +16,10 @@
 // groups, 8 MMAs) pays that cost once per four groups instead of once per two.
 //
 // Layout: a stage holds each operand as K/128 column blocks of 128-byte rows in the
-// canonical 128-byte-swizzled K-major layout (token blocks 128 rows, of which a
-// single tile's token box fills the first M rounded up to 8; weight blocks BN rows).  Tensor memory
-// holds NSET sets of GS accumulators of BN int32 columns.  Roles: warp 0 producer
+// canonical 128-byte-swizzled K-major layout (token blocks 128 rows, of which a single
+// tile's token box fills the first M rounded up to 8; weight blocks BN rows), and
+// packed sub-byte codes in a staging area after them.  Tensor memory holds NSET sets
+// of GS accumulators of BN int32 columns.  Roles: warp 0 producer
 // (lanes 0..KB-1 the token blocks, lanes KB..2KB-1 the weight blocks of a stage, one
 // instruction), warp 1 and the last warp MMA issuers (even and odd stages: one issuing
 // thread is held for each MMA's duration, so one issuer's waits and commits overlap the
