@@ -220,3 +220,25 @@ def test_sweep_table_and_workload():
            "hbm_frac": 0.27, "TOPS": 6.9, "int8_frac": 0.002}
     text = sweep.markdown({"hbm_gbs": 6456.8, "int8_tops": 3021.0, "rows": [row]})
     assert "| W4A8 | qkv | 1 | 14.5 | 1740.0 | 0.27 | 6.9 | 0.002 |" in text
+
+
+def test_reference_arms_of_configs_0_and_1_report_unavailable_without_gpu_work(monkeypatch, capsys):
+    """bench.py --impl reference: config 1 times the reference's own CUDA kernel built
+    into oracle/_ref and prints one `unavailable` line when that module is absent;
+    config 0 (W4A8, which the reference runs on its Triton kernel) always prints one.
+    Neither touches a GPU on those paths."""
+    import json
+    import sys
+    if str(ROOT) not in sys.path:
+        sys.path.insert(0, str(ROOT))
+    import bench
+    from oracle import build_ref
+    monkeypatch.setattr(build_ref, "load", lambda name: None)
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--config", "1"])
+    bench.main()
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and "oracle/_ref" in line["unavailable"]
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--config", "0"])
+    bench.main()
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and "Triton" in line["unavailable"]
